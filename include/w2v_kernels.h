@@ -1,0 +1,118 @@
+/* Internal C-ABI kernel layer of the wav2vec2-b200 engine (sm_100a).
+ *
+ * Plain extern "C" launchers: device pointers, sizes and a cudaStream_t
+ * passed as void*; they return a W2V_* status and never throw.  The C++ host
+ * engine (wav2vec2.cpp_b200/csrc/engine.cpp) calls these; so do the GPU
+ * parity tests, through ctypes.  Each entry names the reference code whose
+ * computation it replaces (paths inside py-ai-dev/wav2vec2.cpp).
+ *
+ * Layouts: packed encoder rows are [M = sum of frames, width] row-major.  Conv
+ * activations are padded per utterance: [n_utt][rows_max][C] fp16.  `err` is
+ * a device int that kernels set (first writer wins) when a bounded wait
+ * expires; it may be NULL.
+ */
+#ifndef W2V_KERNELS_H
+#define W2V_KERNELS_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    W2V_OK = 0,
+    W2V_ERR_ARGS = 1,        /* invalid sizes, strides or alignment */
+    W2V_ERR_LAUNCH = 2,      /* CUDA launch/config error */
+    W2V_ERR_DRIVER = 3,      /* driver entry point unavailable */
+    W2V_ERR_TENSOR_MAP = 4,  /* cuTensorMapEncodeTiled rejected the view */
+    W2V_ERR_DEVICE = 5,      /* kernel reported a device-side error */
+};
+
+/* GEMM epilogues. */
+enum {
+    W2V_EPI_F16 = 0,        /* C(fp16) = acc + bias              */
+    W2V_EPI_F16_GELU = 1,   /* C(fp16) = gelu_tanh(acc + bias)   */
+    W2V_EPI_F32 = 2,        /* C(fp32) = acc + bias              */
+    W2V_EPI_F32_RESID = 3,  /* C(fp32) = acc + bias + resid      */
+};
+
+/* tcgen05 GEMM, C = epi(A . B^T).  Replaces ggml_mul_mat in
+ * GgmlScratch::linear (src/ggml_backend.h:78-120) and the strided conv1d of
+ * the extractor (src/ops.h:76-99) as an implicit GEMM.
+ *   A: fp16 activation rows; batch b, input row i at
+ *      A + b*a_batch_stride + i*a_row_stride (a_rows_in rows per batch, a
+ *      multiple of a_stride).  Output row r of batch b reads, for each of
+ *      a_taps taps, input row r*a_stride + tap, columns 0..a_cin-1
+ *      (a_cin % 64 == 0): K = a_taps * a_cin, ordered tap-major.
+ *      Plain GEMM: a_taps = a_stride = a_batches = 1, a_rows_in = M.
+ *   B: fp16 [N, K] row-major.
+ *   C: row (b, r) at C + (b*c_batch_rows + r)*ldc, written for r < m_valid.
+ *   bias: fp32 [N] or NULL; resid: fp32 rows like C (ldr), may alias C.
+ *   block_n: 0 = automatic, else 64/128/256. */
+int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_stride, long long a_row_stride,
+                 long long a_rows_in, long long a_batches, long long a_batch_stride, const void* B,
+                 int N, void* C, long long ldc, long long c_batch_rows, int m_valid, const float* bias,
+                 const float* resid, long long ldr, int epilogue, int block_n, int* err,
+                 void* stream);
+
+/* Expand GGUF linear weight rows ([N, K], GGUF type F32=0, F16=1, Q4_0=2,
+ * Q8_0=8, raw bytes as stored in the file) to fp16 [N, K].  Block formats as
+ * written by scripts/convert_to_gguf.py:63-97. */
+int w2v_dequant_f16(const void* raw, int gguf_type, long long n_rows, long long K, void* out,
+                    void* stream);
+
+/* Per-utterance waveform statistics (src/wav2vec2.cpp:262-271): stats[2u] =
+ * mean, stats[2u+1] = 1/sqrt(var + 1e-7), population variance. audio is
+ * packed; utterance u is audio[off[u] .. off[u]+len[u]). */
+int w2v_wave_stats(const float* audio, const long long* off, const int* len, int n_utt,
+                   float* stats, void* stream);
+
+/* Conv layer 0 (Cin = 1, kernel k0, stride s0, C channels) on the normalised
+ * waveform, then the layer's norm and GELU (src/wav2vec2.cpp:273-287,
+ * src/ops.h:24-50,76-99).
+ *   norm: 0 = none, 1 = GroupNorm over time per channel (needs gn_sums,
+ *   a device double buffer [n_utt][C][2] that this call zeroes and fills),
+ *   2 = LayerNorm over channels per frame.
+ *   w0: fp32 [C][k0]; b0: fp32 [C] or NULL; gw/gb: fp32 [C] norm affine.
+ *   out: fp16 [n_utt][rows_max][C]; frames per utterance (len-k0)/s0+1. */
+int w2v_conv0(const float* audio, const long long* off, const int* len, const int* frames, int n_utt,
+              const float* stats, const float* w0, const float* b0, int C, int k0, int s0, int norm,
+              const float* gw, const float* gb, double* gn_sums, void* out, long long rows_max,
+              int max_frames, void* stream);
+
+/* Row LayerNorm (eps 1e-5, src/ops.h:24-36) over D columns of fp16 or fp32
+ * rows, optional GELU after the affine, fp32 and/or fp16 outputs.
+ * Input row r of utterance u: in + (u*in_batch_rows + r)*ld_in, r < rows[u]
+ * (rows == NULL: r < n_rows with one batch).  Output rows are packed
+ * (out_off[u] + r) when out_off != NULL, else laid out like the input. */
+int w2v_layer_norm(const void* in, int in_f16, long long ld_in, long long in_batch_rows,
+                   const int* rows, const long long* out_off, int n_batch, int n_rows, int D,
+                   const float* w, const float* b, int gelu, float* out32, void* out16,
+                   long long ld_out, void* stream);
+
+/* Positional conv embedding (src/wav2vec2.cpp:349-356): grouped conv1d over
+ * time (kernel Kp, padding Kp/2, G groups, first T of T+1 outputs), GELU,
+ * added to x in place.  x: fp32 packed rows [M, H]; utterance u occupies rows
+ * off[u] .. off[u]+T[u]; x = xin + gelu(conv(xin) + bias), x != xin.
+ * wt: fp16 weights re-laid out by the engine as [G][Kp][H/G (co)][H/G (ci)];
+ * bias fp32 [H].  H/G must be 32, 48, 64 or 80. */
+int w2v_pos_conv(float* x, const float* xin, const long long* off, const int* T, int n_utt, int H,
+                 int Kp, int G, const void* wt, const float* bias, int max_T, void* stream);
+
+/* Bidirectional multi-head attention (src/wav2vec2.cpp:293-334), flash-style
+ * online softmax in fp32, fp16 tensor-core products.  qkv: fp16 [M, 3H]
+ * (q | k | v, head h at columns h*d..), out: fp16 [M, H].  Keys are limited
+ * to the query's own utterance (rows off[u] .. off[u]+T[u]). */
+int w2v_attention(const void* qkv, void* out, const long long* off, const int* T, int n_utt, int H,
+                  int n_heads, int max_T, void* stream);
+
+/* Greedy CTC (src/ops.h:132-149): per frame argmax (first max wins), run
+ * collapse into spans (id, t_start, t_end), blank runs kept.  logits fp32
+ * packed [M, V]; spans written at spans + 3*off[u]; n_spans[u] = count. */
+int w2v_ctc_greedy(const float* logits, const long long* off, const int* T, int n_utt, int V,
+                   int* ids, int* spans, int* n_spans, int max_T, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

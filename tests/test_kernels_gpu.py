@@ -1,0 +1,262 @@
+"""Per-kernel parity on the GPU, through the C-ABI launchers.
+
+Floating-point kernels are compared with an fp32/fp64 torch or oracle
+computation on the same (fp16-rounded) inputs; integer/index kernels
+(weight expansion, greedy CTC) must be bit-exact."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+EPI_F16, EPI_F16_GELU, EPI_F32, EPI_F32_RESID = 0, 1, 2, 3
+
+
+@pytest.fixture(scope="module")
+def K(pkg):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    import w2v_b200.binding as b
+    b.lib()
+    return b.kernels
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def gelu_t(x):
+    return 0.5 * x * (1.0 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
+
+
+def err_word():
+    return torch.zeros(1, dtype=torch.int32, device="cuda")
+
+
+@pytest.mark.parametrize("M,N,Kd,epi,bn", [
+    (1, 64, 64, EPI_F32, 0), (200, 768, 768, EPI_F16, 0), (1000, 2304, 768, EPI_F16, 0),
+    (777, 3072, 768, EPI_F16_GELU, 0), (333, 768, 3072, EPI_F32_RESID, 0), (499, 32, 768, EPI_F32, 64),
+    (130, 128, 512, EPI_F32, 128), (257, 256, 1024, EPI_F32_RESID, 256), (4100, 1024, 1024, EPI_F32, 0),
+    (99, 64, 768, EPI_F32, 64), (640, 5120, 1280, EPI_F16_GELU, 0)])
+def test_gemm_plain(K, M, N, Kd, epi, bn):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    A = torch.randn(M, Kd, device="cuda", generator=g).half()
+    W = (torch.randn(N, Kd, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(N, device="cuda", generator=g)
+    resid = torch.randn(M, N, device="cuda", generator=g)
+    f16 = epi in (EPI_F16, EPI_F16_GELU)
+    out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float16 if f16 else torch.float32)
+    err = err_word()
+    K.gemm(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, out.data_ptr(), N, M, M, bias.data_ptr(),
+           resid.data_ptr() if epi == EPI_F32_RESID else 0, N, epi, bn, err.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = A.double() @ W.double().T + bias.double()
+    if epi == EPI_F16_GELU:
+        ref = gelu_t(ref)
+    if epi == EPI_F32_RESID:
+        ref = ref + resid.double()
+    d = (out.double() - ref).abs()
+    tol = (2e-3 if f16 else 2e-5) * (1 + ref.abs())
+    assert torch.isfinite(out).all()
+    assert (d <= tol).all(), f"max err {d.max().item()}"
+
+
+@pytest.mark.parametrize("B,C,Lin,k,s", [(3, 128, 257, 3, 2), (2, 512, 1000, 3, 2), (4, 128, 130, 2, 2),
+                                         (1, 64, 77, 3, 2)])
+def test_gemm_conv_view(K, B, C, Lin, k, s):
+    """Strided conv as implicit GEMM over the 4-D TMA view (src/ops.h:76-99)."""
+    g = torch.Generator(device="cuda").manual_seed(Lin)
+    Lout = (Lin - k) // s + 1
+    R = Lin + (-Lin) % s
+    x = torch.randn(B, R, C, device="cuda", generator=g).half()
+    w = (torch.randn(C, C, k, device="cuda", generator=g) * 0.05).half()          # [co][ci][k]
+    wg = w.permute(0, 2, 1).reshape(C, k * C).contiguous()                         # [co][k*C + ci]
+    Rout = Lout + 3
+    out = torch.full((B, Rout, C), float("nan"), device="cuda")
+    err = err_word()
+    K.gemm(x.data_ptr(), C, k, s, C, R, B, R * C, wg.data_ptr(), C, out.data_ptr(), C, Rout, Lout, 0, 0, 0,
+           EPI_F32, 0, err.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = torch.nn.functional.conv1d(x[:, :Lin].double().transpose(1, 2), w.double(), stride=s).transpose(1, 2)
+    d = (out[:, :Lout].double() - ref).abs()
+    assert (d <= 2e-5 * (1 + ref.abs())).all(), d.max().item()
+
+
+def test_gemm_rejects_bad_args(K):
+    a = torch.zeros(64, 96, device="cuda", dtype=torch.float16)   # K not a multiple of 64
+    w = torch.zeros(64, 96, device="cuda", dtype=torch.float16)
+    o = torch.zeros(64, 64, device="cuda")
+    import w2v_b200.binding as b
+    with pytest.raises(b.EngineError):
+        K.gemm(a.data_ptr(), 96, 1, 1, 96, 64, 1, 64 * 96, w.data_ptr(), 64, o.data_ptr(), 64, 64, 64,
+               epilogue=EPI_F32, stream=stream())
+
+
+@pytest.mark.parametrize("dtype", ["q8_0", "q4_0", "f16", "f32"])
+def test_dequant_bit_exact(K, synth, dtype):
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((96, 256)) * 0.02).astype(np.float32)
+    gt, raw = synth.encode_tensor("x.q_proj.weight", w, dtype)
+    if dtype == "f32":
+        gt, raw = synth.GGUF_F32, w.tobytes()
+    ref = synth.dequantize(raw, gt, w.shape).astype(np.float16)
+    d_raw = torch.from_numpy(np.frombuffer(raw, np.uint8).copy()).cuda()
+    out = torch.empty(w.shape, dtype=torch.float16, device="cuda")
+    K.dequant(d_raw.data_ptr(), gt, w.shape[0], w.shape[1], out.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+def _meta(lens, k0=10, s0=5):
+    off = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    frames = np.array([(n - k0) // s0 + 1 if n >= k0 else 0 for n in lens], np.int32)
+    return off, np.array(lens, np.int32), frames
+
+
+@pytest.mark.parametrize("norm", [0, 1, 2])
+def test_conv0_norm_gelu(K, synth, norm):
+    """Waveform normalisation + conv layer 0 + GroupNorm/LayerNorm + GELU
+    (src/wav2vec2.cpp:262-287) against the oracle."""
+    C, k0, s0 = 512, 10, 5
+    lens = [16000, 9000, 3210]
+    audio = [synth.make_audio(n, 40 + i) for i, n in enumerate(lens)]
+    off, ln, frames = _meta(lens)
+    rng = np.random.default_rng(norm)
+    w0 = (rng.standard_normal((C, 1, k0)) * 0.02).astype(np.float32)
+    b0 = (rng.standard_normal(C) * 0.01).astype(np.float32)
+    gw = (1 + rng.standard_normal(C) * 0.1).astype(np.float32)
+    gb = (rng.standard_normal(C) * 0.02).astype(np.float32)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    d_audio, d_off, d_len, d_fr = dev(np.concatenate(audio)), dev(off), dev(ln), dev(frames)
+    stats = torch.empty(2 * len(lens), device="cuda")
+    gn = torch.empty(len(lens) * C * 2, device="cuda", dtype=torch.float64)
+    rows = int(frames.max()) + 5
+    out = torch.zeros(len(lens), rows, C, device="cuda", dtype=torch.float16)
+    K.wave_stats(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), len(lens), stats.data_ptr(), stream())
+    K.conv0(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), d_fr.data_ptr(), len(lens), stats.data_ptr(),
+            dev(w0.reshape(C, k0)).data_ptr(), dev(b0).data_ptr(), C, k0, s0, norm,
+            dev(gw).data_ptr() if norm else 0, dev(gb).data_ptr() if norm else 0,
+            gn.data_ptr() if norm == 1 else 0, out.data_ptr(), rows, int(frames.max()), stream())
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    for u, x in enumerate(audio):
+        xd = x.astype(np.float64)
+        xn = ((x - np.float32(xd.mean())) * np.float32(1 / np.sqrt(np.float32(xd.var()) + 1e-7))).astype(np.float32)
+        y = O.conv1d(xn[:, None], w0, b0, stride=s0)
+        if norm == 1:
+            y = O.group_norm(y, gw, gb)
+        elif norm == 2:
+            y = O.layer_norm(y, gw, gb)
+        ref = np.vectorize(O.gelu)(y) if y.size < 2000 else 0.5 * y * (1 + np.tanh(0.7978845608028654 * (y + 0.044715 * y ** 3)))
+        g_u = got[u, :frames[u]]
+        assert np.abs(g_u - ref).max() <= 2e-3 * (1 + np.abs(ref).max()), np.abs(g_u - ref).max()
+
+
+@pytest.mark.parametrize("D,f16in,gelu", [(768, 0, 0), (512, 1, 1), (1280, 0, 0), (128, 1, 0)])
+def test_layer_norm(K, D, f16in, gelu):
+    rng = np.random.default_rng(D)
+    rows = [37, 0, 100]
+    R = 110
+    x = (rng.standard_normal((3, R, D)) * 2 + 0.5).astype(np.float32)
+    if f16in:
+        x = x.astype(np.float16).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(D)).astype(np.float32)
+    d_in = torch.from_numpy(x.astype(np.float16) if f16in else x).cuda()
+    off = np.array([0, 37, 37], np.int64)
+    M = sum(rows)
+    out32 = torch.zeros(M, D, device="cuda")
+    out16 = torch.zeros(M, D, device="cuda", dtype=torch.float16)
+    K.layer_norm(d_in.data_ptr(), f16in, D, R, torch.tensor(rows, dtype=torch.int32).cuda().data_ptr(),
+                 torch.from_numpy(off).cuda().data_ptr(), 3, 0, D, torch.from_numpy(w).cuda().data_ptr(),
+                 torch.from_numpy(b).cuda().data_ptr(), gelu, out32.data_ptr(), out16.data_ptr(), D, stream())
+    torch.cuda.synchronize()
+    ref = np.concatenate([O.layer_norm(x[u, :rows[u]], w, b) for u in range(3) if rows[u]])
+    if gelu:
+        ref = 0.5 * ref * (1 + np.tanh(0.7978845608028654 * (ref + 0.044715 * ref ** 3)))
+    assert np.abs(out32.cpu().numpy() - ref).max() < 1e-4
+    assert np.abs(out16.float().cpu().numpy() - ref).max() < 2e-3 * (1 + np.abs(ref).max())
+
+
+@pytest.mark.parametrize("H,G,Kp", [(768, 16, 128), (128, 4, 16), (1024, 16, 128), (1280, 16, 128)])
+def test_pos_conv(K, H, G, Kp):
+    """Grouped positional conv + GELU + residual (src/wav2vec2.cpp:349-356)."""
+    rng = np.random.default_rng(H)
+    T = [130, 7, 300]
+    off = np.concatenate([[0], np.cumsum(T)[:-1]]).astype(np.int64)
+    M = sum(T)
+    xin = rng.standard_normal((M, H)).astype(np.float16).astype(np.float32)
+    Cg = H // G
+    w = (rng.standard_normal((H, Cg, Kp)) * 0.02).astype(np.float16).astype(np.float32)
+    b = (rng.standard_normal(H) * 0.1).astype(np.float32)
+    wt = w.reshape(G, Cg, Cg, Kp).transpose(0, 3, 1, 2).astype(np.float16).copy()   # [G][Kp][co][ci]
+    d_x = torch.zeros(M, H, device="cuda")
+    K.pos_conv(d_x.data_ptr(), torch.from_numpy(xin).cuda().data_ptr(), torch.from_numpy(off).cuda().data_ptr(),
+               torch.tensor(T, dtype=torch.int32).cuda().data_ptr(), len(T), H, Kp, G,
+               torch.from_numpy(wt).cuda().data_ptr(), torch.from_numpy(b).cuda().data_ptr(), max(T), stream())
+    torch.cuda.synchronize()
+    got = d_x.cpu().numpy()
+    for u, t in enumerate(T):
+        xs = torch.from_numpy(xin[off[u]:off[u] + t]).double()
+        conv = torch.nn.functional.conv1d(xs.T[None], torch.from_numpy(w).double(), torch.from_numpy(b).double(),
+                                          padding=Kp // 2, groups=G)[0].T[:t]
+        ref = (xs + gelu_t(conv)).numpy()
+        assert np.abs(got[off[u]:off[u] + t] - ref).max() < 2e-4 * (1 + np.abs(ref).max())
+
+
+@pytest.mark.parametrize("H,nh", [(768, 12), (1280, 16), (128, 2)])
+def test_attention(K, H, nh):
+    """Flash attention vs fp64 softmax(QK^T/sqrt(d))V per utterance
+    (src/wav2vec2.cpp:304-334)."""
+    rng = np.random.default_rng(H)
+    T = [499, 1, 64, 65, 200]
+    off = np.concatenate([[0], np.cumsum(T)[:-1]]).astype(np.int64)
+    M = sum(T)
+    qkv = (rng.standard_normal((M, 3 * H)) * 1.5).astype(np.float16)
+    out = torch.zeros(M, H, device="cuda", dtype=torch.float16)
+    K.attention(torch.from_numpy(qkv).cuda().data_ptr(), out.data_ptr(), torch.from_numpy(off).cuda().data_ptr(),
+                torch.tensor(T, dtype=torch.int32).cuda().data_ptr(), len(T), H, nh, max(T), stream())
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    d = H // nh
+    q = torch.from_numpy(qkv[:, :H].astype(np.float64))
+    k = torch.from_numpy(qkv[:, H:2 * H].astype(np.float64))
+    v = torch.from_numpy(qkv[:, 2 * H:].astype(np.float64))
+    for u, t in enumerate(T):
+        sl = slice(off[u], off[u] + t)
+        qh = q[sl].view(t, nh, d).transpose(0, 1)
+        kh = k[sl].view(t, nh, d).transpose(0, 1)
+        vh = v[sl].view(t, nh, d).transpose(0, 1)
+        p = torch.softmax(qh @ kh.transpose(1, 2) / math.sqrt(d), -1)
+        ref = (p @ vh).transpose(0, 1).reshape(t, H).numpy()
+        assert np.abs(got[sl] - ref).max() < 4e-3, np.abs(got[sl] - ref).max()
+
+
+def test_ctc_greedy_bit_exact(K):
+    """Per-frame argmax (first max wins) + run collapse (src/ops.h:132-149)."""
+    rng = np.random.default_rng(9)
+    T, V = [500, 1, 0, 37, 1024], 32
+    off = np.concatenate([[0], np.cumsum(T)[:-1]]).astype(np.int64)
+    M = sum(T)
+    lg = rng.integers(-3, 3, (M, V)).astype(np.float32)      # many ties and long runs
+    lg[10:40, 5] = 9
+    d_lg = torch.from_numpy(lg).cuda()
+    ids = torch.zeros(M, dtype=torch.int32, device="cuda")
+    spans = torch.zeros(3 * M, dtype=torch.int32, device="cuda")
+    ns = torch.zeros(len(T), dtype=torch.int32, device="cuda")
+    K.ctc_greedy(d_lg.data_ptr(), torch.from_numpy(off).cuda().data_ptr(),
+                 torch.tensor(T, dtype=torch.int32).cuda().data_ptr(), len(T), V, ids.data_ptr(), spans.data_ptr(),
+                 ns.data_ptr(), max(T), stream())
+    torch.cuda.synchronize()
+    sp, n = spans.cpu().numpy(), ns.cpu().numpy()
+    for u, t in enumerate(T):
+        ref = O.greedy_spans(lg[off[u]:off[u] + t])
+        got = [tuple(int(v) for v in sp[3 * (off[u] + i): 3 * (off[u] + i) + 3]) for i in range(n[u])]
+        assert got == ref

@@ -1,0 +1,509 @@
+// C API of the wav2vec2-b200 engine (include/wav2vec2.h, include/wav2vec2_b200.h).
+//
+// Mirrors the reference's public API (src/wav2vec2.cpp:458-533): same result
+// layout and ownership (everything malloc'd, released by
+// wav2vec2_result_free), same text post-processing (ids_to_text /
+// spans_to_words, src/wav2vec2.cpp:396-452) and beam search
+// (src/ops.h:151-251) on the host, with the forward pass on the GPU.
+// C++ exceptions never cross this boundary: failures return NULL / a status
+// and leave a message for wav2vec2_b200_last_error().
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "engine.hpp"
+#include "wav2vec2_b200.h"
+
+using namespace w2v;
+
+struct wav2vec2_context {
+    ModelConfig cfg;
+    std::vector<std::unique_ptr<Engine>> engines;
+    int max_batch = 64;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+void set_error(const std::string& e) { g_last_error = e; }
+
+// ── detokenisation (src/wav2vec2.cpp:396-452) ───────────────────────────────
+
+bool is_special(const std::string& s) { return s.size() >= 2 && s.front() == '<' && s.back() == '>'; }
+
+std::string trim_spaces(const std::string& s) {
+    const auto a = s.find_first_not_of(' ');
+    if (a == std::string::npos) return "";
+    const auto b = s.find_last_not_of(' ');
+    return s.substr(a, b - a + 1);
+}
+
+std::string ids_to_text(const std::vector<int>& ids, const ModelConfig& c) {
+    std::string out;
+    for (int id : ids) {
+        if (id == c.pad_id || id < 0 || id >= (int)c.tokens.size()) continue;
+        const auto& tok = c.tokens[id];
+        if (tok == c.word_delim) { out += ' '; continue; }
+        if (is_special(tok)) continue;
+        out += tok;
+    }
+    return trim_spaces(out);
+}
+
+struct Span { int id, t0, t1; };
+struct Word { std::string text; int t0, t1; };
+
+std::vector<Word> spans_to_words(const std::vector<Span>& spans, const ModelConfig& c) {
+    std::vector<Word> words;
+    std::string cur;
+    int s0 = -1, s1 = -1;
+    auto flush = [&]() {
+        if (cur.empty()) return;
+        std::string t = trim_spaces(cur);
+        if (!t.empty()) words.push_back({t, s0, s1});
+        cur.clear();
+        s0 = s1 = -1;
+    };
+    for (const auto& sp : spans) {
+        if (sp.id == c.pad_id || sp.id < 0 || sp.id >= (int)c.tokens.size()) continue;
+        const auto& tok = c.tokens[sp.id];
+        if (is_special(tok)) continue;
+        if (tok == c.word_delim) { flush(); continue; }
+        if (s0 < 0) s0 = sp.t0;
+        s1 = sp.t1;
+        cur += tok;
+    }
+    flush();
+    return words;
+}
+
+// ── prefix beam search (src/ops.h:151-251, Graves 2006, log domain) ─────────
+
+float log_sum_exp(float a, float b) {
+    if (a <= -1e29f) return b;
+    if (b <= -1e29f) return a;
+    const float mx = std::max(a, b);
+    return mx + log1pf(expf(std::min(a, b) - mx));
+}
+
+std::vector<int> beam_search(const float* logits, int T, int V, int blank, int width) {
+    constexpr float kNegInf = -1e30f;
+    struct State {
+        float pb = kNegInf, pnb = kNegInf;
+        float score() const { return log_sum_exp(pb, pnb); }
+    };
+    using Beams = std::map<std::vector<int>, State>;
+    Beams cur;
+    cur[{}].pb = 0.f;
+    std::vector<float> lp(V);
+    for (int t = 0; t < T; t++) {
+        const float* row = logits + (size_t)t * V;
+        const float mx = *std::max_element(row, row + V);
+        float z = 0.f;
+        for (int v = 0; v < V; v++) z += expf(row[v] - mx);
+        const float lz = mx + logf(z);
+        for (int v = 0; v < V; v++) lp[v] = row[v] - lz;
+        Beams next;
+        for (auto& [prefix, st] : cur) {
+            const int last = prefix.empty() ? -1 : prefix.back();
+            {
+                auto& ns = next[prefix];
+                ns.pb = log_sum_exp(ns.pb, log_sum_exp(st.pb, st.pnb) + lp[blank]);
+            }
+            for (int ch = 0; ch < V; ch++) {
+                if (ch == blank) continue;
+                if (ch == last) {
+                    auto& same = next[prefix];
+                    same.pnb = log_sum_exp(same.pnb, st.pnb + lp[ch]);
+                    auto ext = prefix;
+                    ext.push_back(ch);
+                    auto& ns = next[ext];
+                    ns.pnb = log_sum_exp(ns.pnb, st.pb + lp[ch]);
+                } else {
+                    auto ext = prefix;
+                    ext.push_back(ch);
+                    auto& ns = next[ext];
+                    ns.pnb = log_sum_exp(ns.pnb, log_sum_exp(st.pb, st.pnb) + lp[ch]);
+                }
+            }
+        }
+        cur.clear();
+        std::vector<std::pair<float, const std::vector<int>*>> ranked;
+        ranked.reserve(next.size());
+        for (auto& [k, st] : next) ranked.push_back({st.score(), &k});
+        std::sort(ranked.begin(), ranked.end(), [](const auto& a, const auto& b) { return a.first > b.first; });
+        const int keep = std::min((int)ranked.size(), width);
+        for (int i = 0; i < keep; i++) cur[*ranked[i].second] = next[*ranked[i].second];
+    }
+    const std::vector<int>* best = nullptr;
+    float bs = kNegInf;
+    for (auto& [k, st] : cur) {
+        const float s = st.score();
+        if (s > bs) { bs = s; best = &k; }
+    }
+    return best ? *best : std::vector<int>{};
+}
+
+// ── result assembly (src/wav2vec2.cpp:491-532) ──────────────────────────────
+
+char* dup_str(const std::string& s) {
+    char* p = (char*)malloc(s.size() + 1);
+    memcpy(p, s.c_str(), s.size() + 1);
+    return p;
+}
+
+wav2vec2_result* make_result(const ModelConfig& c, int T, const std::string& text, const std::vector<Word>* words) {
+    auto* r = (wav2vec2_result*)calloc(1, sizeof(wav2vec2_result));
+    r->n_frames = T;
+    r->transcript = dup_str(text);
+    if (words && !words->empty()) {
+        r->n_words = (int)words->size();
+        r->words = (wav2vec2_word*)malloc(r->n_words * sizeof(wav2vec2_word));
+        for (int i = 0; i < r->n_words; i++) {
+            const auto& w = (*words)[i];
+            r->words[i].t_start = w.t0 * (320.f / 16000.f);
+            r->words[i].t_end = w.t1 * (320.f / 16000.f);
+            r->words[i].text = dup_str(w.text);
+        }
+    }
+    (void)c;
+    return r;
+}
+
+// Batches of utterance indices: longest first, at most max_batch utterances
+// and a bounded number of samples per batch (length bucketing keeps padding
+// in the conv extractor small).
+std::vector<std::vector<int>> make_batches(const int* n_samples, int n_utt, int max_batch) {
+    std::vector<int> order(n_utt);
+    for (int i = 0; i < n_utt; i++) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return n_samples[a] > n_samples[b]; });
+    const long long budget = (long long)max_batch * 16000LL * 32;   // ~32 s per slot
+    std::vector<std::vector<int>> batches;
+    std::vector<int> cur;
+    long long cur_max = 0;
+    for (int i : order) {
+        const long long n = std::max(n_samples[i], 1);
+        const long long new_max = std::max(cur_max, n);
+        if (!cur.empty() && ((int)cur.size() >= max_batch || new_max * (long long)(cur.size() + 1) > budget)) {
+            batches.push_back(cur);
+            cur.clear();
+            cur_max = 0;
+        }
+        cur.push_back(i);
+        cur_max = std::max(cur_max, n);
+    }
+    if (!cur.empty()) batches.push_back(cur);
+    return batches;
+}
+
+// Run every batch, sharded over the context's devices (one host thread per
+// device pulling from a shared queue); fn(engine, batch index list, logits,
+// spans, n_spans, geometry) consumes each result on the worker thread.
+template <typename Fn>
+void run_sharded(wav2vec2_context* ctx, const float* const* samples, const int* n_samples, int n_utt,
+                 bool want_logits, bool want_spans, Fn fn) {
+    auto batches = make_batches(n_samples, n_utt, ctx->max_batch);
+    std::atomic<size_t> next{0};
+    std::mutex err_mu;
+    std::string first_err;
+    auto worker = [&](Engine* e) {
+        std::vector<float> logits;
+        std::vector<int> spans, nsp;
+        for (;;) {
+            const size_t bi = next.fetch_add(1);
+            if (bi >= batches.size()) break;
+            try {
+                const auto& b = batches[bi];
+                std::vector<const float*> a;
+                std::vector<int> ns;
+                for (int i : b) { a.push_back(samples[i]); ns.push_back(n_samples[i]); }
+                BatchGeom g;
+                e->run_host(a, ns, want_logits ? &logits : nullptr, want_spans ? &spans : nullptr,
+                            want_spans ? &nsp : nullptr, &g);
+                fn(e, b, logits, spans, nsp, g);
+            } catch (const std::exception& ex) {
+                std::lock_guard<std::mutex> lk(err_mu);
+                if (first_err.empty()) first_err = ex.what();
+                next.store(batches.size());
+            }
+        }
+    };
+    if (ctx->engines.size() == 1 || batches.size() <= 1) {
+        worker(ctx->engines[0].get());
+    } else {
+        std::vector<std::thread> th;
+        for (auto& e : ctx->engines) th.emplace_back(worker, e.get());
+        for (auto& t : th) t.join();
+    }
+    if (!first_err.empty()) throw std::runtime_error(first_err);
+}
+
+}  // namespace
+
+// ── public API ──────────────────────────────────────────────────────────────
+
+extern "C" {
+
+const char* wav2vec2_b200_last_error(void) { return g_last_error.c_str(); }
+
+wav2vec2_params wav2vec2_default_params(void) {
+    wav2vec2_params p{};
+    p.n_threads = 4;
+    p.beam_size = 1;
+    p.verbose = false;
+    p.word_timestamps = false;
+    return p;
+}
+
+void wav2vec2_result_free(wav2vec2_result* r) {
+    if (!r) return;
+    free(r->transcript);
+    if (r->words) {
+        for (int i = 0; i < r->n_words; i++) free(r->words[i].text);
+        free(r->words);
+    }
+    free(r);
+}
+
+wav2vec2_context* wav2vec2_b200_init(const char* path, const int* devices, int n_devices, int max_batch) {
+    try {
+        if (!path) throw std::runtime_error("NULL model path");
+        GgufFile gf(path);
+        auto ctx = std::make_unique<wav2vec2_context>();
+        ctx->cfg = ModelConfig::from_gguf(gf);
+        ctx->max_batch = max_batch > 0 ? max_batch : 64;
+        if (n_devices <= 0) n_devices = 1;
+        int avail = 0;
+        if (cudaGetDeviceCount(&avail) != cudaSuccess || avail == 0) throw std::runtime_error("no CUDA device");
+        for (int i = 0; i < n_devices; i++) {
+            const int d = devices ? devices[i] : i;
+            if (d < 0 || d >= avail) throw std::runtime_error("invalid device index " + std::to_string(d));
+            ctx->engines.push_back(std::make_unique<Engine>(gf, ctx->cfg, d));
+        }
+        return ctx.release();
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        fprintf(stderr, "wav2vec2_init: %s\n", e.what());
+        return nullptr;
+    }
+}
+
+wav2vec2_context* wav2vec2_init(const char* path) {
+    int n = 1;
+    if (const char* s = getenv("W2V_N_DEVICES")) n = std::max(1, atoi(s));
+    return wav2vec2_b200_init(path, nullptr, n, 0);
+}
+
+void wav2vec2_free(wav2vec2_context* ctx) { delete ctx; }
+
+int wav2vec2_b200_n_devices(const wav2vec2_context* ctx) { return ctx ? (int)ctx->engines.size() : 0; }
+
+int wav2vec2_b200_model_info(const wav2vec2_context* ctx, int* out) {
+    if (!ctx || !out) return W2V_STATUS_INVALID;
+    const auto& c = ctx->cfg;
+    out[0] = c.conv_dim; out[1] = c.hidden; out[2] = c.n_layers; out[3] = c.n_heads;
+    out[4] = c.ffn; out[5] = c.vocab; out[6] = c.pad_id; out[7] = c.stable ? 1 : 0;
+    return W2V_STATUS_OK;
+}
+
+int wav2vec2_b200_n_frames(const wav2vec2_context* ctx, int n_samples) {
+    return ctx ? ctx->cfg.frames(n_samples) : 0;
+}
+
+int wav2vec2_transcribe_batch(wav2vec2_context* ctx, wav2vec2_params params, const float* const* samples,
+                              const int* n_samples, int n_utt, wav2vec2_result** results) {
+    if (!ctx || (!samples && n_utt > 0) || (!n_samples && n_utt > 0) || !results || n_utt < 0) {
+        set_error("invalid arguments");
+        return W2V_STATUS_INVALID;
+    }
+    for (int i = 0; i < n_utt; i++) {
+        results[i] = nullptr;
+        if (n_samples[i] < 0 || (n_samples[i] > 0 && !samples[i])) {
+            set_error("invalid utterance " + std::to_string(i));
+            return W2V_STATUS_INVALID;
+        }
+    }
+    const auto t_start = std::chrono::steady_clock::now();
+    const ModelConfig& c = ctx->cfg;
+    const bool beam = params.beam_size > 1;
+    try {
+        run_sharded(ctx, samples, n_samples, n_utt, beam, !beam,
+                    [&](Engine*, const std::vector<int>& b, const std::vector<float>& logits,
+                        const std::vector<int>& spans, const std::vector<int>& nsp, const BatchGeom& g) {
+                        // host decoding of this batch with up to n_threads threads
+                        const int nb = (int)b.size();
+                        auto decode = [&](int j) {
+                            const int T = g.T[j];
+                            std::vector<Word> words;
+                            std::string text;
+                            if (beam) {
+                                const float* lg = logits.data() + (size_t)g.T_off[j] * c.vocab;
+                                text = ids_to_text(beam_search(lg, T, c.vocab, c.pad_id, params.beam_size), c);
+                            } else {
+                                std::vector<Span> sp;
+                                std::vector<int> ids;
+                                for (int k = 0; k < (T > 0 ? nsp[j] : 0); k++) {
+                                    const int* s = spans.data() + 3 * ((size_t)g.T_off[j] + k);
+                                    sp.push_back({s[0], s[1], s[2]});
+                                    if (s[0] != c.pad_id) ids.push_back(s[0]);
+                                }
+                                text = ids_to_text(ids, c);
+                                if (params.word_timestamps) words = spans_to_words(sp, c);
+                            }
+                            results[b[j]] = make_result(c, T, text, params.word_timestamps ? &words : nullptr);
+                        };
+                        const int nt = std::max(1, std::min(params.n_threads, nb));
+                        if (nt == 1 || !beam) {
+                            for (int j = 0; j < nb; j++) decode(j);
+                        } else {
+                            std::atomic<int> nx{0};
+                            std::vector<std::thread> th;
+                            for (int t = 0; t < nt; t++)
+                                th.emplace_back([&]() {
+                                    for (int j; (j = nx.fetch_add(1)) < nb;) decode(j);
+                                });
+                            for (auto& t : th) t.join();
+                        }
+                    });
+    } catch (const std::exception& e) {
+        for (int i = 0; i < n_utt; i++) { wav2vec2_result_free(results[i]); results[i] = nullptr; }
+        set_error(e.what());
+        return strstr(e.what(), "device error") ? W2V_STATUS_DEVICE : W2V_STATUS_CUDA;
+    }
+    if (params.verbose) {
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() -
+                                                                              t_start).count();
+        fprintf(stderr, "wav2vec2: %d utterances, %s(b=%d), %lld ms\n", n_utt, beam ? "beam" : "greedy",
+                params.beam_size, (long long)ms);
+    }
+    return W2V_STATUS_OK;
+}
+
+wav2vec2_result* wav2vec2_transcribe(wav2vec2_context* ctx, wav2vec2_params params, const float* samples,
+                                     int n_samples) {
+    wav2vec2_result* r = nullptr;
+    const float* s[1] = {samples};
+    int n[1] = {n_samples};
+    if (wav2vec2_transcribe_batch(ctx, params, s, n, 1, &r) != W2V_STATUS_OK) {
+        fprintf(stderr, "wav2vec2_transcribe: %s\n", g_last_error.c_str());
+        return nullptr;
+    }
+    return r;
+}
+
+int wav2vec2_b200_logits(wav2vec2_context* ctx, const float* const* samples, const int* n_samples, int n_utt,
+                         float* logits, int* n_frames) {
+    if (!ctx || n_utt < 0 || (n_utt > 0 && (!samples || !n_samples || !logits || !n_frames))) {
+        set_error("invalid arguments");
+        return W2V_STATUS_INVALID;
+    }
+    // output row offset of each utterance in input order
+    std::vector<long long> out_off(n_utt + 1, 0);
+    for (int i = 0; i < n_utt; i++) {
+        if (n_samples[i] < 0 || (n_samples[i] > 0 && !samples[i])) { set_error("invalid utterance"); return W2V_STATUS_INVALID; }
+        n_frames[i] = ctx->cfg.frames(n_samples[i]);
+        out_off[i + 1] = out_off[i] + n_frames[i];
+    }
+    const int V = ctx->cfg.vocab;
+    try {
+        run_sharded(ctx, samples, n_samples, n_utt, true, false,
+                    [&](Engine*, const std::vector<int>& b, const std::vector<float>& lg, const std::vector<int>&,
+                        const std::vector<int>&, const BatchGeom& g) {
+                        for (size_t j = 0; j < b.size(); j++)
+                            if (g.T[j] > 0)
+                                memcpy(logits + out_off[b[j]] * V, lg.data() + (size_t)g.T_off[j] * V,
+                                       (size_t)g.T[j] * V * sizeof(float));
+                    });
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return strstr(e.what(), "device error") ? W2V_STATUS_DEVICE : W2V_STATUS_CUDA;
+    }
+    return W2V_STATUS_OK;
+}
+
+int wav2vec2_b200_forward_device(wav2vec2_context* ctx, const float* d_audio, const int* n_samples, int n_utt,
+                                 void* stream) {
+    if (!ctx || n_utt < 0 || (n_utt > 0 && (!d_audio || !n_samples))) {
+        set_error("invalid arguments");
+        return W2V_STATUS_INVALID;
+    }
+    try {
+        Engine* e = ctx->engines[0].get();
+        std::vector<int> ns(n_samples, n_samples + n_utt);
+        BatchGeom g = e->geometry(ns);
+        e->forward(d_audio, g, reinterpret_cast<cudaStream_t>(stream));
+    } catch (const std::exception& ex) {
+        set_error(ex.what());
+        return W2V_STATUS_CUDA;
+    }
+    return W2V_STATUS_OK;
+}
+
+int wav2vec2_b200_device_outputs(wav2vec2_context* ctx, const float** logits, const int** spans,
+                                 const int** n_spans, long long* M) {
+    if (!ctx) return W2V_STATUS_INVALID;
+    Engine* e = ctx->engines[0].get();
+    if (logits) *logits = e->d_logits();
+    if (spans) *spans = e->d_spans();
+    if (n_spans) *n_spans = e->d_n_spans();
+    if (M) *M = e->last_M();
+    return W2V_STATUS_OK;
+}
+
+int wav2vec2_b200_debug_stages(wav2vec2_context* ctx, const float* samples, int n_samples, float* feat,
+                               float* stages, float* logits) {
+    if (!ctx || !samples || n_samples <= 0) {
+        set_error("invalid arguments");
+        return W2V_STATUS_INVALID;
+    }
+    try {
+        Engine* e = ctx->engines[0].get();
+        cudaSetDevice(e->device());
+        BatchGeom g = e->geometry({n_samples});
+        if (g.M == 0) throw std::runtime_error("utterance too short");
+        void* d = nullptr;
+        if (cudaMalloc(&d, (size_t)n_samples * 4) != cudaSuccess) throw std::runtime_error("cudaMalloc");
+        cudaMemcpy(d, samples, (size_t)n_samples * 4, cudaMemcpyHostToDevice);
+        e->forward(static_cast<float*>(d), g, e->stream(), feat, stages);
+        if (logits)
+            cudaMemcpyAsync(logits, e->d_logits(), (size_t)g.M * ctx->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                            e->stream());
+        const cudaError_t err = cudaStreamSynchronize(e->stream());
+        cudaFree(d);
+        if (err != cudaSuccess) throw std::runtime_error(cudaGetErrorString(err));
+        if (e->check_device_error()) throw std::runtime_error("device error (bounded wait expired)");
+    } catch (const std::exception& ex) {
+        set_error(ex.what());
+        return W2V_STATUS_CUDA;
+    }
+    return W2V_STATUS_OK;
+}
+
+int wav2vec2_b200_profile(wav2vec2_context* ctx, int enable) {
+    if (!ctx) return W2V_STATUS_INVALID;
+    for (auto& e : ctx->engines) e->set_profiling(enable != 0);
+    return W2V_STATUS_OK;
+}
+
+int wav2vec2_b200_profile_read(wav2vec2_context* ctx, const char** names, double* ms, long long* launches,
+                               double* flops, int cap) {
+    if (!ctx) return -1;
+    return ctx->engines[0]->profile_read(names, ms, launches, flops, cap);
+}
+
+long long wav2vec2_b200_launches_per_forward(const wav2vec2_context* ctx) {
+    return ctx ? ctx->engines[0]->launches_last_forward() : 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,611 @@
+#include "engine.hpp"
+
+#include <algorithm>
+#include <cstring>
+#include <stdexcept>
+
+#include "w2v_kernels.h"
+
+namespace w2v {
+
+namespace {
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+void w2v_check(int rc, const char* what) {
+    if (rc != W2V_OK) {
+        const cudaError_t e = cudaGetLastError();
+        throw std::runtime_error(std::string(what) + " failed (status " + std::to_string(rc) + ")" +
+                                 (e != cudaSuccess ? std::string(": ") + cudaGetErrorString(e) : std::string()));
+    }
+}
+long long round_up(long long v, long long m) { return (v + m - 1) / m * m; }
+
+}  // namespace
+
+enum ProfCat { P_WAVE, P_CONV0, P_GEMM_CONV, P_LN, P_GEMM_PROJ, P_POSCONV, P_GEMM_ENC, P_ATTN, P_GEMM_LM, P_CTC, P_N };
+static const char* kProfNames[P_N] = {"wave_stats", "conv0", "gemm_conv", "layer_norm", "gemm_proj",
+                                      "pos_conv", "gemm_encoder", "attention", "gemm_lm_head", "ctc_greedy"};
+
+template <typename Fn>
+void Engine::launch(int cat, double flops, cudaStream_t st, const char* what, Fn fn) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (profiling_) {
+        if (ev_pool_.size() < 2) {
+            for (int i = 0; i < 64; i++) {
+                cudaEvent_t e;
+                cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+                ev_pool_.push_back(e);
+            }
+        }
+        a = ev_pool_.back(); ev_pool_.pop_back();
+        b = ev_pool_.back(); ev_pool_.pop_back();
+        cuda_check(cudaEventRecord(a, st), "cudaEventRecord");
+    }
+    w2v_check(fn(), what);
+    launches_cur_++;
+    if (profiling_) {
+        cuda_check(cudaEventRecord(b, st), "cudaEventRecord");
+        prof_pending_.push_back({cat, a, b, flops});
+    }
+}
+
+void Engine::prof_fold() {
+    if (prof_ms_.empty()) { prof_ms_.assign(P_N, 0.0); prof_flops_.assign(P_N, 0.0); prof_n_.assign(P_N, 0); }
+    for (auto& r : prof_pending_) {
+        float ms = 0.f;
+        cudaEventSynchronize(r.b);
+        if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+            prof_ms_[r.cat] += ms;
+            prof_flops_[r.cat] += r.flops;
+            prof_n_[r.cat] += 1;
+        }
+        ev_pool_.push_back(r.a);
+        ev_pool_.push_back(r.b);
+    }
+    prof_pending_.clear();
+}
+
+void Engine::set_profiling(bool on) {
+    cudaSetDevice(device_);
+    prof_fold();
+    profiling_ = on;
+    prof_ms_.assign(P_N, 0.0);
+    prof_flops_.assign(P_N, 0.0);
+    prof_n_.assign(P_N, 0);
+}
+
+int Engine::profile_read(const char** names, double* ms, long long* launches, double* flops, int cap) {
+    cudaSetDevice(device_);
+    prof_fold();
+    int n = std::min<int>(cap, P_N);
+    for (int i = 0; i < n; i++) {
+        if (names) names[i] = kProfNames[i];
+        if (ms) ms[i] = prof_ms_.empty() ? 0.0 : prof_ms_[i];
+        if (launches) launches[i] = prof_n_.empty() ? 0 : prof_n_[i];
+        if (flops) flops[i] = prof_flops_.empty() ? 0.0 : prof_flops_[i];
+    }
+    return n;
+}
+
+// ── model configuration (src/wav2vec2.cpp:133-202) ──────────────────────────
+
+ModelConfig ModelConfig::from_gguf(const GgufFile& gf) {
+    ModelConfig c;
+    c.n_conv = (int)gf.u32("wav2vec2.n_conv_layers");
+    c.conv_dim = (int)gf.u32("wav2vec2.conv_dim");
+    c.n_layers = (int)gf.u32("wav2vec2.n_encoder_layers");
+    c.n_heads = (int)gf.u32("wav2vec2.n_heads");
+    c.hidden = (int)gf.u32("wav2vec2.hidden_size");
+    c.ffn = (int)gf.u32("wav2vec2.intermediate_size");
+    c.vocab = (int)gf.u32("wav2vec2.vocab_size");
+    c.pad_id = (int)gf.u32("wav2vec2.pad_token_id");
+    c.group_norm = gf.str("wav2vec2.feat_extract_norm") == "group";
+    c.pos_k = (int)gf.u32("wav2vec2.pos_conv_kernel");
+    c.pos_g = (int)gf.u32("wav2vec2.pos_conv_groups");
+    for (auto v : gf.arr_u32("wav2vec2.conv_kernel")) c.conv_k.push_back((int)v);
+    for (auto v : gf.arr_u32("wav2vec2.conv_stride")) c.conv_s.push_back((int)v);
+    c.tokens = gf.arr_str("tokenizer.ggml.tokens");
+    c.vocab = (int)c.tokens.size();                       // as the reference (wav2vec2.cpp:150-151)
+    if (gf.has_kv("wav2vec2.word_delimiter_token")) c.word_delim = gf.str("wav2vec2.word_delimiter_token");
+    c.stable = gf.has_kv("wav2vec2.stable_layer_norm") && gf.u32("wav2vec2.stable_layer_norm") != 0;
+    if ((int)c.conv_k.size() < c.n_conv || (int)c.conv_s.size() < c.n_conv || c.n_conv < 1)
+        throw std::runtime_error("conv_kernel/conv_stride shorter than n_conv_layers");
+    for (int i = 0; i < c.n_conv; i++) {
+        const std::string p = "feature_extractor.conv_layers." + std::to_string(i);
+        c.conv_norm.push_back(gf.has(p + ".layer_norm.weight"));
+        c.conv_bias.push_back(gf.has(p + ".conv.bias"));
+    }
+    // Shapes the kernels support (all published wav2vec2 / XLS-R models fit).
+    auto need = [](bool ok, const std::string& what) {
+        if (!ok) throw std::runtime_error("unsupported model: " + what);
+    };
+    need(c.conv_dim % 64 == 0 && c.conv_dim <= 512, "conv_dim must be a multiple of 64, <= 512");
+    need(c.hidden % 64 == 0 && c.ffn % 64 == 0, "hidden and intermediate sizes must be multiples of 64");
+    need(c.n_heads > 0 && c.hidden % c.n_heads == 0, "hidden not divisible by n_heads");
+    const int d = c.n_heads ? c.hidden / c.n_heads : 0;
+    need(d == 64 || d == 80 || d == 128, "head dim must be 64, 80 or 128");
+    need(c.pos_g > 0 && c.hidden % c.pos_g == 0, "hidden not divisible by pos_conv_groups");
+    const int cg = c.pos_g ? c.hidden / c.pos_g : 0;
+    need(cg == 32 || cg == 48 || cg == 64 || cg == 80, "hidden/pos_conv_groups must be 32, 48, 64 or 80");
+    need(c.pos_k > 0 && c.pos_k % 2 == 0, "pos_conv_kernel must be even");
+    need(c.conv_k[0] <= 16, "first conv kernel must be <= 16");
+    for (int i = 1; i < c.n_conv; i++)
+        need(!(c.conv_norm[i] && c.group_norm), "GroupNorm is supported on conv layer 0 only");
+    need(c.vocab > 0, "empty vocabulary");
+    return c;
+}
+
+int ModelConfig::frames(long long n) const {
+    long long L = n;
+    for (int i = 0; i < n_conv; i++) {
+        if (L < conv_k[i]) return 0;
+        L = (L - conv_k[i]) / conv_s[i] + 1;
+    }
+    return (int)L;
+}
+
+// ── device buffers ──────────────────────────────────────────────────────────
+
+void DevBuf::ensure(size_t bytes) {
+    if (bytes <= n) return;
+    release();
+    cuda_check(cudaMalloc(&p, bytes), "cudaMalloc");
+    n = bytes;
+}
+void DevBuf::release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+}
+
+// ── load ────────────────────────────────────────────────────────────────────
+
+Engine::Engine(const GgufFile& gf, const ModelConfig& cfg, int device) : cfg_(cfg), device_(device) {
+    cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+    cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    cuda_check(cudaEventCreateWithFlags(&meta_done_, cudaEventDisableTiming), "cudaEventCreate");
+    err_.ensure(sizeof(int));
+    cuda_check(cudaMemset(err_.p, 0, sizeof(int)), "cudaMemset");
+    load(gf);
+    cuda_check(cudaStreamSynchronize(stream_), "weight upload");
+}
+
+Engine::~Engine() {
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    auto rel = [](DevBuf& b) { b.release(); };
+    for (DevBuf* b : {&conv0_w_, &conv0_b_, &proj_lnw_, &proj_lnb_, &proj_w_, &proj_b_, &pos_w_, &pos_b_, &enc_lnw_,
+                      &enc_lnb_, &lm_w_, &lm_b_, &audio_stage_, &meta_, &stats_, &gn_, &actA_, &actB_, &feat_,
+                      &pbuf_, &x_, &xh_, &qkv_, &attn_, &hbuf_, &ybuf_, &logits_, &ids_, &spans_, &nspans_, &err_})
+        rel(*b);
+    for (auto* v : {&conv_w_, &conv_b_, &conv_gw_, &conv_gb_})
+        for (auto& b : *v) rel(b);
+    for (auto& L : layers_)
+        for (DevBuf* b : {&L.wqkv, &L.bqkv, &L.wo, &L.bo, &L.w1, &L.b1, &L.w2, &L.b2, &L.ln1w, &L.ln1b, &L.ln2w,
+                          &L.ln2b})
+            rel(*b);
+    if (h_audio_) cudaFreeHost(h_audio_);
+    prof_fold();
+    for (auto e : ev_pool_) cudaEventDestroy(e);
+    if (meta_done_) cudaEventDestroy(meta_done_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+static void upload_floats(DevBuf& d, const std::vector<float>& v) {
+    d.ensure(v.size() * sizeof(float));
+    cuda_check(cudaMemcpy(d.p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice), "upload");
+}
+
+static std::vector<float> floats_sized(const GgufFile& gf, const std::string& name, size_t n) {
+    auto v = gf.floats(name);
+    if (v.size() != n) throw std::runtime_error("tensor size mismatch: " + name);
+    return v;
+}
+
+// fp32 host data -> fp16 device buffer (via a temporary fp32 upload).
+static void upload_f16(DevBuf& d, const std::vector<float>& v, cudaStream_t st) {
+    DevBuf tmp;
+    upload_floats(tmp, v);
+    d.ensure(v.size() * 2);
+    w2v_check(w2v_dequant_f16(tmp.p, 0, 1, (long long)v.size(), d.p, st), "fp16 weight conversion");
+    cuda_check(cudaStreamSynchronize(st), "fp16 weight conversion");
+    tmp.release();
+}
+
+void Engine::upload_linear(const GgufFile& gf, const std::string& name, int N, int K, DevBuf& w,
+                           size_t row_offset) {
+    const auto& t = gf.tensor(name + ".weight");
+    // GGUF dims are innermost first: [K, N] (src/wav2vec2.cpp:116-125)
+    if (t.shape.size() < 2 || (int)t.shape[0] != K || (int)t.shape[1] != N)
+        throw std::runtime_error("tensor shape mismatch: " + name + ".weight");
+    if (t.type != GT_F32 && t.type != GT_F16 && t.type != GT_Q8_0 && t.type != GT_Q4_0)
+        throw std::runtime_error("unsupported weight type " + std::to_string(t.type) + " for " + name);
+    if (t.nbytes != gguf_nbytes(t.type, (uint64_t)N * K))
+        throw std::runtime_error("tensor size mismatch: " + name + ".weight");
+    DevBuf raw;
+    raw.ensure(t.nbytes);
+    cuda_check(cudaMemcpy(raw.p, t.data, t.nbytes, cudaMemcpyHostToDevice), "weight upload");
+    w2v_check(w2v_dequant_f16(raw.p, (int)t.type, N, K, static_cast<uint16_t*>(w.p) + row_offset * K, stream_),
+              "weight expansion");
+    cuda_check(cudaStreamSynchronize(stream_), "weight expansion");
+    raw.release();
+}
+
+void Engine::load(const GgufFile& gf) {
+    const ModelConfig& c = cfg_;
+    const int C = c.conv_dim, H = c.hidden, F = c.ffn, V = c.vocab;
+    // conv layer 0: [C][1][k0] fp32 (src/wav2vec2.cpp:182-202)
+    upload_floats(conv0_w_, floats_sized(gf, "feature_extractor.conv_layers.0.conv.weight", (size_t)C * c.conv_k[0]));
+    conv_w_.resize(c.n_conv);
+    conv_b_.resize(c.n_conv);
+    conv_gw_.resize(c.n_conv);
+    conv_gb_.resize(c.n_conv);
+    for (int i = 0; i < c.n_conv; i++) {
+        const std::string p = "feature_extractor.conv_layers." + std::to_string(i);
+        if (c.conv_bias[i]) upload_floats(conv_b_[i], floats_sized(gf, p + ".conv.bias", C));
+        if (c.conv_norm[i]) {
+            upload_floats(conv_gw_[i], floats_sized(gf, p + ".layer_norm.weight", C));
+            upload_floats(conv_gb_[i], floats_sized(gf, p + ".layer_norm.bias", C));
+        }
+        if (i == 0) continue;
+        // [co][ci][k] -> implicit-GEMM B operand [co][k*C + ci]
+        const int K = c.conv_k[i];
+        auto w = floats_sized(gf, p + ".conv.weight", (size_t)C * C * K);
+        std::vector<float> r((size_t)C * C * K);
+        for (int co = 0; co < C; co++)
+            for (int ci = 0; ci < C; ci++)
+                for (int k = 0; k < K; k++) r[((size_t)co * K + k) * C + ci] = w[((size_t)co * C + ci) * K + k];
+        upload_f16(conv_w_[i], r, stream_);
+    }
+    // feature projection (src/wav2vec2.cpp:205-208)
+    upload_floats(proj_lnw_, floats_sized(gf, "feature_projection.layer_norm.weight", C));
+    upload_floats(proj_lnb_, floats_sized(gf, "feature_projection.layer_norm.bias", C));
+    proj_w_.ensure((size_t)H * C * 2);
+    upload_linear(gf, "feature_projection.projection", H, C, proj_w_);
+    upload_floats(proj_b_, floats_sized(gf, "feature_projection.projection.bias", H));
+    // positional conv [H][Cg][Kp] -> [G][Kp][co][ci] (src/wav2vec2.cpp:211-212)
+    {
+        const int G = c.pos_g, Cg = H / G, Kp = c.pos_k;
+        auto w = floats_sized(gf, "encoder.pos_conv_embed.conv.weight", (size_t)H * Cg * Kp);
+        std::vector<float> r(w.size());
+        for (int g = 0; g < G; g++)
+            for (int oc = 0; oc < Cg; oc++)
+                for (int ic = 0; ic < Cg; ic++)
+                    for (int k = 0; k < Kp; k++)
+                        r[(((size_t)g * Kp + k) * Cg + oc) * Cg + ic] = w[((size_t)(g * Cg + oc) * Cg + ic) * Kp + k];
+        upload_f16(pos_w_, r, stream_);
+        upload_floats(pos_b_, floats_sized(gf, "encoder.pos_conv_embed.conv.bias", H));
+    }
+    upload_floats(enc_lnw_, floats_sized(gf, "encoder.layer_norm.weight", H));
+    upload_floats(enc_lnb_, floats_sized(gf, "encoder.layer_norm.bias", H));
+    // encoder layers (src/wav2vec2.cpp:219-242); Q, K, V stacked into one [3H, H]
+    layers_.resize(c.n_layers);
+    for (int l = 0; l < c.n_layers; l++) {
+        auto& L = layers_[l];
+        const std::string p = "encoder.layers." + std::to_string(l);
+        L.wqkv.ensure((size_t)3 * H * H * 2);
+        upload_linear(gf, p + ".attention.q_proj", H, H, L.wqkv, 0);
+        upload_linear(gf, p + ".attention.k_proj", H, H, L.wqkv, (size_t)H);
+        upload_linear(gf, p + ".attention.v_proj", H, H, L.wqkv, (size_t)2 * H);
+        std::vector<float> bq = floats_sized(gf, p + ".attention.q_proj.bias", H);
+        auto bk = floats_sized(gf, p + ".attention.k_proj.bias", H);
+        auto bv = floats_sized(gf, p + ".attention.v_proj.bias", H);
+        bq.insert(bq.end(), bk.begin(), bk.end());
+        bq.insert(bq.end(), bv.begin(), bv.end());
+        upload_floats(L.bqkv, bq);
+        L.wo.ensure((size_t)H * H * 2);
+        upload_linear(gf, p + ".attention.out_proj", H, H, L.wo);
+        upload_floats(L.bo, floats_sized(gf, p + ".attention.out_proj.bias", H));
+        L.w1.ensure((size_t)F * H * 2);
+        upload_linear(gf, p + ".feed_forward.intermediate_dense", F, H, L.w1);
+        upload_floats(L.b1, floats_sized(gf, p + ".feed_forward.intermediate_dense.bias", F));
+        L.w2.ensure((size_t)H * F * 2);
+        upload_linear(gf, p + ".feed_forward.output_dense", H, F, L.w2);
+        upload_floats(L.b2, floats_sized(gf, p + ".feed_forward.output_dense.bias", H));
+        upload_floats(L.ln1w, floats_sized(gf, p + ".layer_norm.weight", H));
+        upload_floats(L.ln1b, floats_sized(gf, p + ".layer_norm.bias", H));
+        upload_floats(L.ln2w, floats_sized(gf, p + ".final_layer_norm.weight", H));
+        upload_floats(L.ln2b, floats_sized(gf, p + ".final_layer_norm.bias", H));
+    }
+    // CTC head (src/wav2vec2.cpp:245-246)
+    lm_w_.ensure((size_t)V * H * 2);
+    upload_linear(gf, "lm_head", V, H, lm_w_);
+    upload_floats(lm_b_, floats_sized(gf, "lm_head.bias", V));
+}
+
+// ── per-batch geometry and workspace ────────────────────────────────────────
+
+BatchGeom Engine::geometry(const std::vector<int>& n_samples) const {
+    const ModelConfig& c = cfg_;
+    BatchGeom g;
+    g.n_utt = (int)n_samples.size();
+    g.n_samples = n_samples;
+    g.L.assign(c.n_conv, std::vector<int>(g.n_utt, 0));
+    g.Lmax.assign(c.n_conv, 0);
+    long long off = 0;
+    for (int u = 0; u < g.n_utt; u++) {
+        if (n_samples[u] < 0) throw std::runtime_error("negative sample count");
+        g.audio_off.push_back(off);
+        off += n_samples[u];
+        long long L = n_samples[u];
+        for (int i = 0; i < c.n_conv; i++) {
+            L = (L < c.conv_k[i]) ? 0 : (L - c.conv_k[i]) / c.conv_s[i] + 1;
+            g.L[i][u] = (int)L;
+            g.Lmax[i] = std::max(g.Lmax[i], (int)L);
+        }
+    }
+    // rows per utterance of each layer's padded buffer: a multiple of the next
+    // layer's stride (the implicit GEMM reads rows in stride-phase groups)
+    g.R.resize(c.n_conv);
+    for (int i = 0; i < c.n_conv; i++) {
+        const long long s_next = i + 1 < c.n_conv ? c.conv_s[i + 1] : 1;
+        g.R[i] = std::max<long long>(round_up(std::max(g.Lmax[i], 1), s_next), s_next);
+    }
+    g.T = g.L.back();
+    g.T_off.resize(g.n_utt);
+    long long m = 0;
+    for (int u = 0; u < g.n_utt; u++) {
+        g.T_off[u] = m;
+        m += g.T[u];
+        g.T_max = std::max(g.T_max, g.T[u]);
+    }
+    g.M = m;
+    return g;
+}
+
+void Engine::ensure_workspace(const BatchGeom& g) {
+    const ModelConfig& c = cfg_;
+    const size_t B = (size_t)std::max(g.n_utt, 1), C = c.conv_dim, H = c.hidden, F = c.ffn, V = c.vocab;
+    const size_t M = (size_t)std::max<long long>(g.M, 1);
+    size_t a0 = 0, a1 = 0;
+    for (int i = 0; i < c.n_conv; i++) {
+        size_t& a = (i % 2) ? a1 : a0;
+        a = std::max<size_t>(a, B * (size_t)g.R[i] * C * 2);
+    }
+    actA_.ensure(std::max<size_t>(a0, 16));
+    actB_.ensure(std::max<size_t>(a1, 16));
+    stats_.ensure(B * 2 * sizeof(float));
+    gn_.ensure(B * C * 2 * sizeof(double));
+    feat_.ensure(M * C * 2);
+    pbuf_.ensure(M * H * 4);
+    x_.ensure(M * H * 4);
+    ybuf_.ensure(M * H * 4);
+    xh_.ensure(M * H * 2);
+    attn_.ensure(M * H * 2);
+    qkv_.ensure(M * 3 * H * 2);
+    hbuf_.ensure(M * F * 2);
+    logits_.ensure(M * V * 4);
+    ids_.ensure(M * 4);
+    spans_.ensure(M * 3 * 4);
+    nspans_.ensure(B * 4);
+    meta_.ensure(B * (8 + 8 + 4 + 4 + 4 * (size_t)c.n_conv) + 64);
+}
+
+void Engine::upload_meta(const BatchGeom& g, cudaStream_t st) {
+    const int B = g.n_utt, nc = cfg_.n_conv;
+    const size_t bytes = (size_t)B * (8 + 8 + 4 + 4 + 4 * (size_t)nc);
+    cuda_check(cudaEventSynchronize(meta_done_), "meta staging");
+    if (meta_host_.size() < bytes) meta_host_.resize(bytes);
+    uint8_t* h = meta_host_.data();
+    size_t o = 0;
+    auto put = [&](const void* src, size_t n) { memcpy(h + o, src, n); o += n; };
+    put(g.audio_off.data(), 8 * (size_t)B);
+    put(g.T_off.data(), 8 * (size_t)B);
+    put(g.n_samples.data(), 4 * (size_t)B);
+    for (int i = 0; i < nc; i++) put(g.L[i].data(), 4 * (size_t)B);
+    uint8_t* d = meta_.as<uint8_t>();
+    d_audio_off_ = reinterpret_cast<long long*>(d);
+    d_T_off_ = reinterpret_cast<long long*>(d + 8 * (size_t)B);
+    d_len_ = reinterpret_cast<int*>(d + 16 * (size_t)B);
+    d_L_.resize(nc);
+    for (int i = 0; i < nc; i++) d_L_[i] = reinterpret_cast<int*>(d + (20 + 4 * (size_t)i) * B);
+    d_T_ = d_L_[nc - 1];
+    // pageable source: the copy is staged before cudaMemcpyAsync returns
+    cuda_check(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st), "meta upload");
+    cuda_check(cudaEventRecord(meta_done_, st), "meta event");
+}
+
+int Engine::check_device_error() {
+    int e = 0;
+    cudaSetDevice(device_);
+    if (cudaMemcpy(&e, err_.p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (e) cudaMemset(err_.p, 0, sizeof(int));
+    return e;
+}
+
+// ── forward ─────────────────────────────────────────────────────────────────
+
+void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, float* dbg_feat, float* dbg_stages) {
+    if (!st) st = stream_;
+    cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+    const ModelConfig& c = cfg_;
+    const int B = g.n_utt, C = c.conv_dim, H = c.hidden, F = c.ffn, V = c.vocab;
+    last_M_ = g.M;
+    launches_cur_ = 0;
+    if (B == 0) { launches_last_ = 0; return; }
+    ensure_workspace(g);
+    upload_meta(g, st);
+    int* err = err_.as<int>();
+    const long long M = g.M;
+    if (M == 0) {
+        cuda_check(cudaMemsetAsync(nspans_.p, 0, sizeof(int) * B, st), "memset");
+        launches_last_ = 0;
+        return;
+    }
+    auto gemm = [&](int cat, const void* A, long long cin, int taps, int stride, long long row_stride,
+                    long long rows_in, long long batches, long long batch_stride, const void* W, int N, void* out,
+                    long long ldc, long long c_batch_rows, int m_valid, const void* bias, const float* resid, int epi,
+                    double flops, int bn = 0) {
+        launch(cat, flops, st, "gemm", [&] {
+            return w2v_gemm_f16(A, cin, taps, stride, row_stride, rows_in, batches, batch_stride, W, N, out, ldc,
+                                c_batch_rows, m_valid, static_cast<const float*>(bias), resid, ldc, epi, bn, err, st);
+        });
+    };
+    auto plain_gemm = [&](int cat, const void* A, int K, const void* W, int N, void* out, const void* bias,
+                          const float* resid, int epi, int bn = 0) {
+        gemm(cat, A, K, 1, 1, K, M, 1, M * K, W, N, out, N, M, (int)M, bias, resid, epi, 2.0 * M * N * K, bn);
+    };
+    auto dbg_copy = [&](int block, const float* src) {
+        if (!dbg_stages) return;
+        cuda_check(cudaMemcpyAsync(dbg_stages + (size_t)block * M * H, src, (size_t)M * H * 4, cudaMemcpyDeviceToHost,
+                                   st),
+                   "debug copy");
+        cuda_check(cudaStreamSynchronize(st), "debug copy");
+    };
+    long long n_audio = 0;
+    for (int u = 0; u < B; u++) n_audio += g.n_samples[u];
+
+    // 1. waveform normalisation statistics + conv layer 0 with its norm and GELU
+    launch(P_WAVE, 0.0, st, "wave_stats",
+           [&] { return w2v_wave_stats(d_audio, d_audio_off_, d_len_, B, stats_.as<float>(), st); });
+    const int norm0 = c.conv_norm[0] ? (c.group_norm ? 1 : 2) : 0;
+    long long f0 = 0;
+    for (int u = 0; u < B; u++) f0 += g.L[0][u];
+    launch(P_CONV0, 2.0 * f0 * C * c.conv_k[0] * (norm0 == 1 ? 2 : 1), st, "conv0", [&] {
+        return w2v_conv0(d_audio, d_audio_off_, d_len_, d_L_[0], B, stats_.as<float>(), conv0_w_.as<float>(),
+                         c.conv_bias[0] ? conv_b_[0].as<float>() : nullptr, C, c.conv_k[0], c.conv_s[0], norm0,
+                         c.conv_norm[0] ? conv_gw_[0].as<float>() : nullptr,
+                         c.conv_norm[0] ? conv_gb_[0].as<float>() : nullptr, gn_.as<double>(), actA_.p, g.R[0],
+                         g.Lmax[0], st);
+    });
+    if (norm0 == 1) launches_cur_++;   // the GroupNorm statistics pass is a second kernel
+    // 2. conv layers 1..n-1 as implicit GEMMs over the strided windows
+    void* cur = actA_.p;
+    void* nxt = actB_.p;
+    for (int i = 1; i < c.n_conv; i++) {
+        const bool ln = c.conv_norm[i];
+        long long rows = 0;
+        for (int u = 0; u < B; u++) rows += g.L[i][u];
+        if (g.Lmax[i] > 0)
+            gemm(P_GEMM_CONV, cur, C, c.conv_k[i], c.conv_s[i], C, g.R[i - 1], B, g.R[i - 1] * C, conv_w_[i].p, C, nxt,
+                 C, g.R[i], g.Lmax[i], c.conv_bias[i] ? conv_b_[i].p : nullptr, nullptr,
+                 ln ? W2V_EPI_F16 : W2V_EPI_F16_GELU, 2.0 * rows * C * C * c.conv_k[i]);
+        if (ln)
+            launch(P_LN, 0.0, st, "conv layer_norm", [&] {
+                return w2v_layer_norm(nxt, 1, C, g.R[i], d_L_[i], nullptr, B, 0, C, conv_gw_[i].as<float>(),
+                                      conv_gb_[i].as<float>(), 1, nullptr, nxt, C, st);
+            });
+        std::swap(cur, nxt);
+    }
+    if (dbg_feat) {
+        std::vector<uint16_t> tmp((size_t)g.T[0] * C);
+        cuda_check(cudaMemcpyAsync(tmp.data(), cur, tmp.size() * 2, cudaMemcpyDeviceToHost, st), "debug copy");
+        cuda_check(cudaStreamSynchronize(st), "debug copy");
+        for (size_t i = 0; i < tmp.size(); i++) dbg_feat[i] = f16_to_f32(tmp[i]);
+    }
+    // 3. feature projection: LN(conv_dim) -> packed fp16 rows -> linear
+    //    (src/wav2vec2.cpp:345-347)
+    launch(P_LN, 0.0, st, "projection layer_norm", [&] {
+        return w2v_layer_norm(cur, 1, C, g.R[c.n_conv - 1], d_T_, d_T_off_, B, 0, C, proj_lnw_.as<float>(),
+                              proj_lnb_.as<float>(), 0, nullptr, feat_.p, C, st);
+    });
+    plain_gemm(P_GEMM_PROJ, feat_.p, C, proj_w_.p, H, pbuf_.p, proj_b_.p, nullptr, W2V_EPI_F32);
+    dbg_copy(0, pbuf_.as<float>());
+    // 4. positional conv embedding + residual (src/wav2vec2.cpp:349-356)
+    float* x = x_.as<float>();
+    launch(P_POSCONV, 2.0 * M * c.pos_k * (H / c.pos_g) * H, st, "pos_conv", [&] {
+        return w2v_pos_conv(x, pbuf_.as<float>(), d_T_off_, d_T_, B, H, c.pos_k, c.pos_g, pos_w_.p,
+                            pos_b_.as<float>(), g.T_max, st);
+    });
+    const int n_heads = c.n_heads;
+    double attn_flops = 0;
+    for (int u = 0; u < B; u++) attn_flops += 4.0 * g.T[u] * g.T[u] * H;
+    auto ln_rows = [&](const float* in, float* out32, void* out16, const DevBuf& w, const DevBuf& b) {
+        launch(P_LN, 0.0, st, "layer_norm", [&] {
+            return w2v_layer_norm(in, 0, H, M, nullptr, nullptr, 1, (int)M, H, w.as<float>(), b.as<float>(), 0,
+                                  out32, out16, H, st);
+        });
+    };
+    auto attention = [&] {
+        launch(P_ATTN, attn_flops, st, "attention",
+               [&] { return w2v_attention(qkv_.p, attn_.p, d_T_off_, d_T_, B, H, n_heads, g.T_max, st); });
+    };
+    if (!c.stable) {
+        // post-LN encoder (src/wav2vec2.cpp:360-373)
+        ln_rows(x, x, xh_.p, enc_lnw_, enc_lnb_);
+        dbg_copy(1, x);
+        for (int l = 0; l < c.n_layers; l++) {
+            const auto& L = layers_[l];
+            plain_gemm(P_GEMM_ENC, xh_.p, H, L.wqkv.p, 3 * H, qkv_.p, L.bqkv.p, nullptr, W2V_EPI_F16);
+            attention();
+            plain_gemm(P_GEMM_ENC, attn_.p, H, L.wo.p, H, ybuf_.p, L.bo.p, x, W2V_EPI_F32_RESID);
+            ln_rows(ybuf_.as<float>(), x, xh_.p, L.ln1w, L.ln1b);
+            plain_gemm(P_GEMM_ENC, xh_.p, H, L.w1.p, F, hbuf_.p, L.b1.p, nullptr, W2V_EPI_F16_GELU);
+            plain_gemm(P_GEMM_ENC, hbuf_.p, F, L.w2.p, H, ybuf_.p, L.b2.p, x, W2V_EPI_F32_RESID);
+            ln_rows(ybuf_.as<float>(), x, xh_.p, L.ln2w, L.ln2b);
+            dbg_copy(2 + l, x);
+        }
+    } else {
+        // pre-LN ("stable layer norm") encoder (src/wav2vec2.cpp:374-392)
+        dbg_copy(1, x);
+        for (int l = 0; l < c.n_layers; l++) {
+            const auto& L = layers_[l];
+            ln_rows(x, nullptr, xh_.p, L.ln1w, L.ln1b);
+            plain_gemm(P_GEMM_ENC, xh_.p, H, L.wqkv.p, 3 * H, qkv_.p, L.bqkv.p, nullptr, W2V_EPI_F16);
+            attention();
+            plain_gemm(P_GEMM_ENC, attn_.p, H, L.wo.p, H, x, L.bo.p, x, W2V_EPI_F32_RESID);
+            ln_rows(x, nullptr, xh_.p, L.ln2w, L.ln2b);
+            plain_gemm(P_GEMM_ENC, xh_.p, H, L.w1.p, F, hbuf_.p, L.b1.p, nullptr, W2V_EPI_F16_GELU);
+            plain_gemm(P_GEMM_ENC, hbuf_.p, F, L.w2.p, H, x, L.b2.p, x, W2V_EPI_F32_RESID);
+            if (l == c.n_layers - 1) ln_rows(x, x, xh_.p, enc_lnw_, enc_lnb_);
+            dbg_copy(2 + l, x);
+        }
+        if (c.n_layers == 0) ln_rows(x, x, xh_.p, enc_lnw_, enc_lnb_);
+    }
+    // 5. CTC head + greedy decode (src/wav2vec2.cpp:489, 498-503)
+    plain_gemm(P_GEMM_LM, xh_.p, H, lm_w_.p, V, logits_.p, lm_b_.p, nullptr, W2V_EPI_F32, 64);
+    launch(P_CTC, 0.0, st, "ctc_greedy", [&] {
+        return w2v_ctc_greedy(logits_.as<float>(), d_T_off_, d_T_, B, V, ids_.as<int>(), spans_.as<int>(),
+                              nspans_.as<int>(), g.T_max, st);
+    });
+    (void)n_audio;
+    launches_last_ = launches_cur_;
+}
+
+void Engine::run_host(const std::vector<const float*>& audio, const std::vector<int>& n_samples,
+                      std::vector<float>* logits, std::vector<int>* spans, std::vector<int>* n_spans,
+                      BatchGeom* geom_out) {
+    cuda_check(cudaSetDevice(device_), "cudaSetDevice");
+    BatchGeom g = geometry(n_samples);
+    const size_t total = g.n_utt ? (size_t)(g.audio_off.back() + n_samples.back()) : 0;
+    if (total > h_audio_n_) {
+        cuda_check(cudaStreamSynchronize(stream_), "sync");
+        if (h_audio_) cudaFreeHost(h_audio_);
+        h_audio_ = nullptr;
+        cuda_check(cudaMallocHost(&h_audio_, std::max<size_t>(total, 1) * sizeof(float)), "cudaMallocHost");
+        h_audio_n_ = total;
+    }
+    for (int u = 0; u < g.n_utt; u++)
+        if (n_samples[u]) memcpy(h_audio_ + g.audio_off[u], audio[u], (size_t)n_samples[u] * sizeof(float));
+    audio_stage_.ensure(std::max<size_t>(total, 1) * sizeof(float));
+    cuda_check(cudaMemcpyAsync(audio_stage_.p, h_audio_, total * sizeof(float), cudaMemcpyHostToDevice, stream_),
+               "audio upload");
+    forward(audio_stage_.as<float>(), g, stream_);
+    if (g.M > 0) {
+        if (logits) {
+            logits->resize((size_t)g.M * cfg_.vocab);
+            cuda_check(cudaMemcpyAsync(logits->data(), logits_.p, logits->size() * 4, cudaMemcpyDeviceToHost, stream_),
+                       "logits download");
+        }
+        if (spans) {
+            spans->resize((size_t)g.M * 3);
+            cuda_check(cudaMemcpyAsync(spans->data(), spans_.p, spans->size() * 4, cudaMemcpyDeviceToHost, stream_),
+                       "spans download");
+        }
+    }
+    if (n_spans) {
+        n_spans->assign(g.n_utt, 0);
+        if (g.M > 0)
+            cuda_check(cudaMemcpyAsync(n_spans->data(), nspans_.p, (size_t)g.n_utt * 4, cudaMemcpyDeviceToHost,
+                                       stream_),
+                       "spans download");
+    }
+    cuda_check(cudaStreamSynchronize(stream_), "forward");
+    const int e = check_device_error();
+    if (e) throw std::runtime_error("device error " + std::to_string(e) + " (bounded wait expired)");
+    if (geom_out) *geom_out = std::move(g);
+}
+
+}  // namespace w2v

@@ -1,0 +1,161 @@
+// wav2vec2-b200 engine: one model replica on one CUDA device.
+//
+// Owns the device weights (repacked once at load) and the per-batch device
+// workspace, and runs the batched forward pass -- waveform normalisation,
+// conv extractor, feature projection, positional conv, post-LN or pre-LN
+// encoder, CTC head, greedy CTC -- as a fixed sequence of kernel launches on
+// one stream (reference: src/wav2vec2.cpp:257-394, 477-506).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf.hpp"
+
+namespace w2v {
+
+struct ModelConfig {
+    int n_conv = 0, conv_dim = 0, n_layers = 0, n_heads = 0, hidden = 0, ffn = 0, vocab = 0, pad_id = 0;
+    int pos_k = 0, pos_g = 0;
+    bool group_norm = true;       // feat_extract_norm == "group"
+    bool stable = false;          // pre-LN encoder (stable_layer_norm)
+    std::vector<int> conv_k, conv_s;
+    std::vector<bool> conv_norm, conv_bias;
+    std::vector<std::string> tokens;
+    std::string word_delim = "|";
+
+    static ModelConfig from_gguf(const GgufFile& gf);
+    // Frames after the conv stack for n samples (reference wav2vec2.cpp:278); 0 if too short.
+    int frames(long long n_samples) const;
+};
+
+// Device buffer that only grows.
+struct DevBuf {
+    void* p = nullptr;
+    size_t n = 0;
+    void ensure(size_t bytes);
+    void release();
+    template <typename T> T* as() const { return static_cast<T*>(p); }
+};
+
+struct LayerWeights {
+    DevBuf wqkv, bqkv, wo, bo, w1, b1, w2, b2, ln1w, ln1b, ln2w, ln2b;
+};
+
+// Everything one forward pass needs per batch.
+struct BatchGeom {
+    int n_utt = 0;
+    std::vector<int> n_samples;            // per utterance
+    std::vector<long long> audio_off;      // packed audio offsets
+    std::vector<std::vector<int>> L;       // [layer][utt] frames after conv layer
+    std::vector<int> Lmax;                 // per layer
+    std::vector<long long> R;              // per layer: rows per utterance in the padded buffer
+    std::vector<int> T;                    // encoder frames per utterance (= L.back())
+    std::vector<long long> T_off;          // packed row offsets
+    long long M = 0;                       // total frames
+    int T_max = 0;
+};
+
+class Engine {
+public:
+    Engine(const GgufFile& gf, const ModelConfig& cfg, int device);
+    ~Engine();
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
+
+    const ModelConfig& cfg() const { return cfg_; }
+    int device() const { return device_; }
+    cudaStream_t stream() const { return stream_; }
+
+    BatchGeom geometry(const std::vector<int>& n_samples) const;
+
+    // Forward for a batch whose packed audio is in device memory.  Enqueues on
+    // `st` (nullptr: the engine's stream) and returns without synchronising.
+    // If dbg_feat/dbg_stages are non-null (single-utterance debug), copies the
+    // extractor output and per-stage encoder activations to the host
+    // (synchronous).
+    void forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, float* dbg_feat = nullptr,
+                 float* dbg_stages = nullptr);
+
+    // Host-memory convenience used by the C API: packs the utterances into
+    // pinned memory, uploads, runs forward, downloads logits and/or spans.
+    void run_host(const std::vector<const float*>& audio, const std::vector<int>& n_samples,
+                  std::vector<float>* logits, std::vector<int>* spans, std::vector<int>* n_spans,
+                  BatchGeom* geom_out);
+
+    // Outputs of the last forward (device).
+    const float* d_logits() const { return logits_.as<float>(); }
+    const int* d_spans() const { return spans_.as<int>(); }
+    const int* d_n_spans() const { return nspans_.as<int>(); }
+    long long last_M() const { return last_M_; }
+
+    // Device error word set by kernels whose bounded waits expired.
+    int check_device_error();
+
+    // Per-category kernel timing with CUDA events on the forward stream.
+    // Categories: see kProfNames in engine.cpp.  set_profiling resets totals.
+    void set_profiling(bool on);
+    // Synchronises the stream, folds recorded events into the totals and
+    // returns the number of categories written (<= cap).
+    int profile_read(const char** names, double* ms, long long* launches, double* flops, int cap);
+    long long launches_last_forward() const { return launches_last_; }
+
+private:
+    void load(const GgufFile& gf);
+    void upload_linear(const GgufFile& gf, const std::string& name, int N, int K, DevBuf& w,
+                       size_t row_offset = 0);
+    void ensure_workspace(const BatchGeom& g);
+    void upload_meta(const BatchGeom& g, cudaStream_t st);
+    // Launch bookkeeping: counts the launch and, when profiling, brackets it
+    // with events attributed to category `cat` with `flops` algorithmic FLOPs.
+    template <typename Fn> void launch(int cat, double flops, cudaStream_t st, const char* what, Fn fn);
+    void prof_fold();
+
+    ModelConfig cfg_;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+
+    // weights
+    DevBuf conv0_w_, conv0_b_;
+    std::vector<DevBuf> conv_w_, conv_b_, conv_gw_, conv_gb_;
+    DevBuf proj_lnw_, proj_lnb_, proj_w_, proj_b_;
+    DevBuf pos_w_, pos_b_, enc_lnw_, enc_lnb_;
+    std::vector<LayerWeights> layers_;
+    DevBuf lm_w_, lm_b_;
+
+    // workspace
+    DevBuf audio_stage_;                       // device copy of packed audio (run_host)
+    DevBuf meta_;                              // packed per-batch metadata
+    DevBuf stats_, gn_;
+    DevBuf actA_, actB_;                       // fp16 conv ping-pong
+    DevBuf feat_, pbuf_, x_, xh_, qkv_, attn_, hbuf_, ybuf_;
+    DevBuf logits_, ids_, spans_, nspans_;
+    DevBuf err_;
+    long long last_M_ = 0;
+    long long launches_cur_ = 0, launches_last_ = 0;
+
+    struct ProfRec { int cat; cudaEvent_t a, b; double flops; };
+    bool profiling_ = false;
+    std::vector<cudaEvent_t> ev_pool_;
+    std::vector<ProfRec> prof_pending_;
+    std::vector<double> prof_ms_, prof_flops_;
+    std::vector<long long> prof_n_;
+
+    // pinned host staging
+    float* h_audio_ = nullptr;
+    size_t h_audio_n_ = 0;
+    std::vector<uint8_t> meta_host_;
+    cudaEvent_t meta_done_ = nullptr;
+
+    // device pointers into meta_
+    long long* d_audio_off_ = nullptr;
+    int* d_len_ = nullptr;
+    std::vector<int*> d_L_;
+    int* d_T_ = nullptr;
+    long long* d_T_off_ = nullptr;
+};
+
+}  // namespace w2v

@@ -1,0 +1,412 @@
+// Bandwidth-bound kernels around the GEMMs: weight expansion at load time,
+// waveform statistics, conv layer 0 with its norm + GELU, row LayerNorm and
+// the greedy CTC decoder.
+#include "common.cuh"
+#include "w2v_kernels.h"
+
+namespace w2v {
+
+// ── weight expansion (GGUF blocks -> fp16 rows) ─────────────────────────────
+// Q8_0: 34-byte blocks {fp16 d, int8 q[32]}, w = d*q.  Q4_0: 18-byte blocks
+// {fp16 d, 16 bytes}, byte j = elem j (low nibble) | elem j+16 (high), w =
+// d*(q-8)  (scripts/convert_to_gguf.py:63-97).  d*q is exact in fp32 and
+// rounded once to fp16.
+__global__ void dequant_q_kernel(const uint8_t* __restrict__ raw, int type, long long n_blocks,
+                                 __half* __restrict__ out) {
+    const long long blk = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= n_blocks) return;
+    float v[32];
+    if (type == 8) {
+        const uint8_t* b = raw + blk * 34;
+        const float d = __half2float(__ushort_as_half((uint16_t)(b[0] | (b[1] << 8))));
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = d * (float)(int8_t)b[2 + j];
+    } else {
+        const uint8_t* b = raw + blk * 18;
+        const float d = __half2float(__ushort_as_half((uint16_t)(b[0] | (b[1] << 8))));
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            v[j] = d * (float)((int)(b[2 + j] & 0xF) - 8);
+            v[j + 16] = d * (float)((int)(b[2 + j] >> 4) - 8);
+        }
+    }
+    uint4* o = reinterpret_cast<uint4*>(out + blk * 32);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        uint4 u;
+        u.x = pack_half2(v[8 * j + 0], v[8 * j + 1]);
+        u.y = pack_half2(v[8 * j + 2], v[8 * j + 3]);
+        u.z = pack_half2(v[8 * j + 4], v[8 * j + 5]);
+        u.w = pack_half2(v[8 * j + 6], v[8 * j + 7]);
+        o[j] = u;
+    }
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ in, long long n, __half* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __float2half_rn(in[i]);
+}
+
+// ── waveform statistics (src/wav2vec2.cpp:262-271) ──────────────────────────
+template <typename T>
+W2V_DEV T block_sum(T v, T* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    T s = 0;
+    for (int i = 0; i < nw; i++) s += red[i];
+    return s;
+}
+
+__global__ void wave_stats_kernel(const float* __restrict__ audio, const long long* __restrict__ off,
+                                  const int* __restrict__ len, float* __restrict__ stats) {
+    __shared__ double red[32];
+    const int u = blockIdx.x;
+    const float* x = audio + off[u];
+    const int n = len[u];
+    double s = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+    const double mean_d = block_sum(s, red) / n;
+    const float mean = (float)mean_d;
+    double v = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double d = (double)(x[i] - mean);
+        v += d * d;
+    }
+    const float var = (float)(block_sum(v, red) / n);
+    if (threadIdx.x == 0) {
+        stats[2 * u] = mean;
+        stats[2 * u + 1] = 1.f / sqrtf(var + 1e-7f);
+    }
+}
+
+// ── conv layer 0 + norm + GELU (src/wav2vec2.cpp:273-287) ────────────────────
+// Block: 256 threads, each owning channels (2t, 2t+1) of C = 512 (C <= 512,
+// even); kFrames output frames per block.  The normalised samples the block
+// needs are staged in shared memory.
+constexpr int kC0Frames = 32;
+constexpr int kC0MaxK = 16;
+
+struct Conv0Args {
+    const float* audio; const long long* off; const int* len; const int* frames;
+    const float* stats; const float* w0; const float* b0; int C, k0, s0, norm;
+    const float* gw; const float* gb; double* gn; __half* out; long long rows_max;
+};
+
+W2V_DEV void conv0_compute(const Conv0Args& a, const float* xs, int f, int c, float& y0, float& y1,
+                           const float* w_s) {
+    float s0 = a.b0 ? __ldg(a.b0 + c) : 0.f, s1 = a.b0 ? __ldg(a.b0 + c + 1) : 0.f;
+    const float* x = xs + f * a.s0;
+    for (int k = 0; k < a.k0; k++) {
+        s0 += x[k] * w_s[c * a.k0 + k];
+        s1 += x[k] * w_s[(c + 1) * a.k0 + k];
+    }
+    y0 = s0; y1 = s1;
+}
+
+// stats pass (GroupNorm only): per-channel sum and sum of squares over frames.
+__global__ void conv0_gn_stats_kernel(Conv0Args a, int frames_per_block) {
+    extern __shared__ float sh[];
+    float* w_s = sh;                                  // [C][k0]
+    float* xs = sh + a.C * a.k0;                      // samples
+    const int u = blockIdx.y;
+    const int F = a.frames[u];
+    const int f0 = blockIdx.x * frames_per_block;
+    if (f0 >= F) return;
+    const int nf = min(frames_per_block, F - f0);
+    for (int i = threadIdx.x; i < a.C * a.k0; i += blockDim.x) w_s[i] = a.w0[i];
+    const float mean = a.stats[2 * u], inv = a.stats[2 * u + 1];
+    const float* x = a.audio + a.off[u];
+    const int ns = (nf - 1) * a.s0 + a.k0;
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) xs[i] = (x[f0 * a.s0 + i] - mean) * inv;
+    __syncthreads();
+    const int c = 2 * threadIdx.x;
+    if (c >= a.C) return;
+    double s0 = 0, s1 = 0, q0 = 0, q1 = 0;
+    for (int f = 0; f < nf; f++) {
+        float y0, y1;
+        conv0_compute(a, xs, f, c, y0, y1, w_s);
+        s0 += y0; s1 += y1; q0 += (double)y0 * y0; q1 += (double)y1 * y1;
+    }
+    double* g = a.gn + ((long long)u * a.C + c) * 2;
+    atomicAdd(g + 0, s0); atomicAdd(g + 1, q0);
+    atomicAdd(g + 2, s1); atomicAdd(g + 3, q1);
+}
+
+__global__ void conv0_apply_kernel(Conv0Args a) {
+    extern __shared__ float sh[];
+    float* w_s = sh;
+    float* xs = sh + a.C * a.k0;
+    __shared__ float red[8][kC0Frames];
+    __shared__ float rowstat[2][kC0Frames];
+    const int u = blockIdx.y;
+    const int F = a.frames[u];
+    const int f0 = blockIdx.x * kC0Frames;
+    if (f0 >= F) return;
+    const int nf = min(kC0Frames, F - f0);
+    for (int i = threadIdx.x; i < a.C * a.k0; i += blockDim.x) w_s[i] = a.w0[i];
+    const float mean = a.stats[2 * u], inv = a.stats[2 * u + 1];
+    const float* x = a.audio + a.off[u];
+    const int ns = (nf - 1) * a.s0 + a.k0;
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) xs[i] = (x[f0 * a.s0 + i] - mean) * inv;
+    __syncthreads();
+    const int c = 2 * threadIdx.x;
+    const bool active = c < a.C;
+    float y[kC0Frames][2];
+#pragma unroll
+    for (int f = 0; f < kC0Frames; f++) {
+        y[f][0] = y[f][1] = 0.f;
+        if (active && f < nf) conv0_compute(a, xs, f, c, y[f][0], y[f][1], w_s);
+    }
+    if (a.norm == 1 && active) {
+        // GroupNorm (one group per channel) over all frames of the utterance
+        // (src/ops.h:39-50); statistics from the stats pass.
+        const double* g = a.gn + ((long long)u * a.C + c) * 2;
+        float m[2], iv[2];
+        for (int j = 0; j < 2; j++) {
+            const double mu = g[2 * j] / F;
+            const float var = (float)fmax(g[2 * j + 1] / F - mu * mu, 0.0);
+            m[j] = (float)mu;
+            iv[j] = 1.f / sqrtf(var + 1e-5f);
+        }
+#pragma unroll
+        for (int f = 0; f < kC0Frames; f++)
+            for (int j = 0; j < 2; j++) y[f][j] = (y[f][j] - m[j]) * iv[j] * a.gw[c + j] + a.gb[c + j];
+    } else if (a.norm == 2) {
+        // LayerNorm over channels per frame (src/ops.h:24-36), two-pass.
+        const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+        for (int pass = 0; pass < 2; pass++) {
+#pragma unroll
+            for (int f = 0; f < kC0Frames; f++) {
+                float v = 0.f;
+                if (active) {
+                    if (pass == 0) v = y[f][0] + y[f][1];
+                    else { const float d0 = y[f][0] - rowstat[0][f], d1 = y[f][1] - rowstat[0][f]; v = d0 * d0 + d1 * d1; }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (l == 0) red[w][f] = v;
+            }
+            __syncthreads();
+            if (threadIdx.x < kC0Frames) {
+                float s = 0.f;
+                for (int i = 0; i < (int)(blockDim.x >> 5); i++) s += red[i][threadIdx.x];
+                if (pass == 0) rowstat[0][threadIdx.x] = s / a.C;
+                else rowstat[1][threadIdx.x] = 1.f / sqrtf(s / a.C + 1e-5f);
+            }
+            __syncthreads();
+        }
+        if (active) {
+#pragma unroll
+            for (int f = 0; f < kC0Frames; f++)
+                for (int j = 0; j < 2; j++)
+                    y[f][j] = (y[f][j] - rowstat[0][f]) * rowstat[1][f] * a.gw[c + j] + a.gb[c + j];
+        }
+    }
+    if (!active) return;
+#pragma unroll
+    for (int f = 0; f < kC0Frames; f++) {
+        if (f < nf) {
+            __half2 h = __floats2half2_rn(gelu_tanh(y[f][0]), gelu_tanh(y[f][1]));
+            *reinterpret_cast<__half2*>(a.out + ((long long)u * a.rows_max + f0 + f) * a.C + c) = h;
+        }
+    }
+}
+
+// ── row LayerNorm (src/ops.h:24-36), warp per row ───────────────────────────
+template <int MAXV>
+__global__ void layer_norm_kernel(const void* __restrict__ in, int in_f16, long long ld_in, long long in_batch_rows,
+                                  const int* __restrict__ rows, const long long* __restrict__ out_off,
+                                  int n_batch, int n_rows, int D, const float* __restrict__ w,
+                                  const float* __restrict__ b, int gelu, float* __restrict__ out32,
+                                  __half* __restrict__ out16, long long ld_out) {
+    const int warps = blockDim.x >> 5;
+    const long long gw = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const long long rows_per_b = rows ? in_batch_rows : n_rows;
+    const long long bi = gw / rows_per_b, r = gw % rows_per_b;
+    if (bi >= n_batch) return;
+    if (r >= (rows ? rows[bi] : n_rows)) return;
+    const long long irow = bi * in_batch_rows + r;
+    const long long orow = out_off ? out_off[bi] + r : irow;
+    float v[MAXV];
+    const int per = D / 32;   // D % 32 == 0, per <= MAXV
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; i++) {
+        if (i < per) {
+            const int col = lane + 32 * i;
+            v[i] = in_f16 ? __half2float(reinterpret_cast<const __half*>(in)[irow * ld_in + col])
+                          : reinterpret_cast<const float*>(in)[irow * ld_in + col];
+            s += v[i];
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / D;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; i++)
+        if (i < per) { const float d = v[i] - mean; q += d * d; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float inv = 1.f / sqrtf(q / D + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < MAXV; i++) {
+        if (i < per) {
+            const int col = lane + 32 * i;
+            float y = (v[i] - mean) * inv * w[col] + b[col];
+            if (gelu) y = gelu_tanh(y);
+            if (out32) out32[orow * ld_out + col] = y;
+            if (out16) out16[orow * ld_out + col] = __float2half_rn(y);
+        }
+    }
+}
+
+// ── greedy CTC (src/ops.h:132-149) ───────────────────────────────────────────
+// One block per utterance: per-frame argmax (strict >, first max wins), then a
+// block-wide scan over run starts to emit spans {id, t_start, t_end}.
+__global__ void ctc_greedy_kernel(const float* __restrict__ logits, const long long* __restrict__ off,
+                                  const int* __restrict__ Tn, int V, int* __restrict__ ids,
+                                  int* __restrict__ spans, int* __restrict__ n_spans) {
+    __shared__ int warp_tot[32];
+    __shared__ int carry_s;
+    const int u = blockIdx.x;
+    const int T = Tn[u];
+    const long long base = off[u];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    // pass 1: argmax per frame
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const float* row = logits + (base + t) * V;
+        int best = 0;
+        float bv = row[0];
+        for (int v = 1; v < V; v++) {
+            const float x = row[v];
+            if (x > bv) { bv = x; best = v; }
+        }
+        ids[base + t] = best;
+    }
+    if (threadIdx.x == 0) carry_s = 0;
+    __syncthreads();
+    // pass 2: run starts -> span index by exclusive scan
+    for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+        const int t = t0 + threadIdx.x;
+        const int flag = (t < T) && (t == 0 || ids[base + t] != ids[base + t - 1]);
+        int incl = flag;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) warp_tot[w] = incl;
+        __syncthreads();
+        int wbase = 0;
+        for (int i = 0; i < w; i++) wbase += warp_tot[i];
+        const int carry = carry_s;
+        if (flag) {
+            const int si = carry + wbase + incl - 1;
+            spans[3 * (base + si)] = ids[base + t];
+            spans[3 * (base + si) + 1] = t;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int tot = 0;
+            for (int i = 0; i < nw; i++) tot += warp_tot[i];
+            carry_s = carry + tot;
+        }
+        __syncthreads();
+    }
+    const int ns = carry_s;
+    // pass 3: span ends = next span start (or T)
+    for (int i = threadIdx.x; i < ns; i += blockDim.x)
+        spans[3 * (base + i) + 2] = (i + 1 < ns) ? spans[3 * (base + i + 1) + 1] : T;
+    if (threadIdx.x == 0) n_spans[u] = ns;
+}
+
+}  // namespace w2v
+
+using namespace w2v;
+
+static cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+static int launch_rc() { return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH; }
+
+extern "C" int w2v_dequant_f16(const void* raw, int type, long long n_rows, long long K, void* out, void* stream) {
+    if (n_rows <= 0 || K <= 0) return W2V_ERR_ARGS;
+    const long long n = n_rows * K;
+    if (type == 1) {
+        return cudaMemcpyAsync(out, raw, n * 2, cudaMemcpyDeviceToDevice, S(stream)) == cudaSuccess ? W2V_OK
+                                                                                                    : W2V_ERR_LAUNCH;
+    }
+    if (type == 0) {
+        f32_to_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, S(stream)>>>((const float*)raw, n, (__half*)out);
+        return launch_rc();
+    }
+    if ((type != 2 && type != 8) || K % 32) return W2V_ERR_ARGS;
+    const long long nb = n / 32;
+    dequant_q_kernel<<<(unsigned)((nb + 127) / 128), 128, 0, S(stream)>>>((const uint8_t*)raw, type, nb,
+                                                                          (__half*)out);
+    return launch_rc();
+}
+
+extern "C" int w2v_wave_stats(const float* audio, const long long* off, const int* len, int n_utt, float* stats,
+                              void* stream) {
+    if (n_utt <= 0) return W2V_OK;
+    wave_stats_kernel<<<n_utt, 512, 0, S(stream)>>>(audio, off, len, stats);
+    return launch_rc();
+}
+
+extern "C" int w2v_conv0(const float* audio, const long long* off, const int* len, const int* frames, int n_utt,
+                         const float* stats, const float* w0, const float* b0, int C, int k0, int s0, int norm,
+                         const float* gw, const float* gb, double* gn_sums, void* out, long long rows_max,
+                         int max_frames, void* stream) {
+    if (C > 512 || C % 2 || k0 > kC0MaxK || k0 <= 0 || s0 <= 0 || norm < 0 || norm > 2) return W2V_ERR_ARGS;
+    if ((norm == 1 && !gn_sums) || (norm && (!gw || !gb))) return W2V_ERR_ARGS;
+    if (n_utt <= 0 || max_frames <= 0) return W2V_OK;
+    Conv0Args a{audio, off, len, frames, stats, w0, b0, C, k0, s0, norm, gw, gb, gn_sums, (__half*)out, rows_max};
+    if (norm == 1) {
+        cudaMemsetAsync(gn_sums, 0, sizeof(double) * 2 * C * (size_t)n_utt, S(stream));
+        const int fpb = 512;
+        const size_t sh = (size_t)(C * k0 + (fpb - 1) * s0 + k0) * sizeof(float);
+        dim3 g((max_frames + fpb - 1) / fpb, n_utt);
+        conv0_gn_stats_kernel<<<g, 256, sh, S(stream)>>>(a, fpb);
+        int rc = launch_rc();
+        if (rc) return rc;
+    }
+    const size_t sh = (size_t)(C * k0 + (kC0Frames - 1) * s0 + k0) * sizeof(float);
+    dim3 g((max_frames + kC0Frames - 1) / kC0Frames, n_utt);
+    conv0_apply_kernel<<<g, 256, sh, S(stream)>>>(a);
+    return launch_rc();
+}
+
+extern "C" int w2v_layer_norm(const void* in, int in_f16, long long ld_in, long long in_batch_rows, const int* rows,
+                              const long long* out_off, int n_batch, int n_rows, int D, const float* w,
+                              const float* b, int gelu, float* out32, void* out16, long long ld_out,
+                              void* stream) {
+    if (D % 32 || D > 64 * 32 || D <= 0) return W2V_ERR_ARGS;
+    const long long total = rows ? (long long)n_batch * in_batch_rows : (long long)n_rows;
+    if (total <= 0) return W2V_OK;
+    const int warps = 8;
+    const unsigned grid = (unsigned)((total + warps - 1) / warps);
+    const int nb = rows ? n_batch : 1;
+    if (D <= 16 * 32)
+        layer_norm_kernel<16><<<grid, warps * 32, 0, S(stream)>>>(in, in_f16, ld_in, in_batch_rows, rows, out_off,
+                                                                  nb, n_rows, D, w, b, gelu, out32,
+                                                                  (__half*)out16, ld_out);
+    else
+        layer_norm_kernel<64><<<grid, warps * 32, 0, S(stream)>>>(in, in_f16, ld_in, in_batch_rows, rows, out_off,
+                                                                  nb, n_rows, D, w, b, gelu, out32,
+                                                                  (__half*)out16, ld_out);
+    return launch_rc();
+}
+
+extern "C" int w2v_ctc_greedy(const float* logits, const long long* off, const int* T, int n_utt, int V, int* ids,
+                              int* spans, int* n_spans, int max_T, void* stream) {
+    if (V <= 0) return W2V_ERR_ARGS;
+    if (n_utt <= 0) return W2V_OK;
+    (void)max_T;
+    ctc_greedy_kernel<<<n_utt, 256, 0, S(stream)>>>(logits, off, T, V, ids, spans, n_spans);
+    return launch_rc();
+}
