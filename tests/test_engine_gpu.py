@@ -141,7 +141,7 @@ class _DevArray:
     """Wrap a raw device pointer for torch.as_tensor (CUDA array interface)."""
 
     def __init__(self, ptr, n, typestr):
-        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, True), "version": 2}
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 2}
 
 
 def test_forward_device_outputs(W, model_path, synth):

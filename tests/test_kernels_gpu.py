@@ -34,6 +34,12 @@ def gelu_t(x):
     return 0.5 * x * (1.0 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
 
 
+def dev(a):
+    """Device copy of a numpy array.  Callers keep the returned tensor alive
+    until the kernel that uses its pointer has completed."""
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
 def err_word():
     return torch.zeros(1, dtype=torch.int32, device="cuda")
 
@@ -62,7 +68,8 @@ def test_gemm_plain(K, M, N, Kd, epi, bn):
     if epi == EPI_F32_RESID:
         ref = ref + resid.double()
     d = (out.double() - ref).abs()
-    tol = (2e-3 if f16 else 2e-5) * (1 + ref.abs())
+    # fp32 accumulation inside the tensor core over K products
+    tol = (2e-3 if f16 else 1e-4) * (1 + ref.abs())
     assert torch.isfinite(out).all()
     assert (d <= tol).all(), f"max err {d.max().item()}"
 
@@ -133,16 +140,16 @@ def test_conv0_norm_gelu(K, synth, norm):
     b0 = (rng.standard_normal(C) * 0.01).astype(np.float32)
     gw = (1 + rng.standard_normal(C) * 0.1).astype(np.float32)
     gb = (rng.standard_normal(C) * 0.02).astype(np.float32)
-    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
     d_audio, d_off, d_len, d_fr = dev(np.concatenate(audio)), dev(off), dev(ln), dev(frames)
+    d_w0, d_b0, d_gw, d_gb = dev(w0.reshape(C, k0)), dev(b0), dev(gw), dev(gb)
     stats = torch.empty(2 * len(lens), device="cuda")
     gn = torch.empty(len(lens) * C * 2, device="cuda", dtype=torch.float64)
     rows = int(frames.max()) + 5
     out = torch.zeros(len(lens), rows, C, device="cuda", dtype=torch.float16)
     K.wave_stats(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), len(lens), stats.data_ptr(), stream())
     K.conv0(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), d_fr.data_ptr(), len(lens), stats.data_ptr(),
-            dev(w0.reshape(C, k0)).data_ptr(), dev(b0).data_ptr(), C, k0, s0, norm,
-            dev(gw).data_ptr() if norm else 0, dev(gb).data_ptr() if norm else 0,
+            d_w0.data_ptr(), d_b0.data_ptr(), C, k0, s0, norm,
+            d_gw.data_ptr() if norm else 0, d_gb.data_ptr() if norm else 0,
             gn.data_ptr() if norm == 1 else 0, out.data_ptr(), rows, int(frames.max()), stream())
     torch.cuda.synchronize()
     got = out.float().cpu().numpy()
@@ -174,9 +181,10 @@ def test_layer_norm(K, D, f16in, gelu):
     M = sum(rows)
     out32 = torch.zeros(M, D, device="cuda")
     out16 = torch.zeros(M, D, device="cuda", dtype=torch.float16)
-    K.layer_norm(d_in.data_ptr(), f16in, D, R, torch.tensor(rows, dtype=torch.int32).cuda().data_ptr(),
-                 torch.from_numpy(off).cuda().data_ptr(), 3, 0, D, torch.from_numpy(w).cuda().data_ptr(),
-                 torch.from_numpy(b).cuda().data_ptr(), gelu, out32.data_ptr(), out16.data_ptr(), D, stream())
+    d_rows, d_off = dev(np.array(rows, np.int32)), dev(off)
+    d_w, d_b = dev(w), dev(b)
+    K.layer_norm(d_in.data_ptr(), f16in, D, R, d_rows.data_ptr(), d_off.data_ptr(), 3, 0, D, d_w.data_ptr(),
+                 d_b.data_ptr(), gelu, out32.data_ptr(), out16.data_ptr(), D, stream())
     torch.cuda.synchronize()
     ref = np.concatenate([O.layer_norm(x[u, :rows[u]], w, b) for u in range(3) if rows[u]])
     if gelu:
@@ -198,9 +206,9 @@ def test_pos_conv(K, H, G, Kp):
     b = (rng.standard_normal(H) * 0.1).astype(np.float32)
     wt = w.reshape(G, Cg, Cg, Kp).transpose(0, 3, 1, 2).astype(np.float16).copy()   # [G][Kp][co][ci]
     d_x = torch.zeros(M, H, device="cuda")
-    K.pos_conv(d_x.data_ptr(), torch.from_numpy(xin).cuda().data_ptr(), torch.from_numpy(off).cuda().data_ptr(),
-               torch.tensor(T, dtype=torch.int32).cuda().data_ptr(), len(T), H, Kp, G,
-               torch.from_numpy(wt).cuda().data_ptr(), torch.from_numpy(b).cuda().data_ptr(), max(T), stream())
+    d_xin, d_off, d_T, d_wt, d_b = dev(xin), dev(off), dev(np.array(T, np.int32)), dev(wt), dev(b)
+    K.pos_conv(d_x.data_ptr(), d_xin.data_ptr(), d_off.data_ptr(), d_T.data_ptr(), len(T), H, Kp, G,
+               d_wt.data_ptr(), d_b.data_ptr(), max(T), stream())
     torch.cuda.synchronize()
     got = d_x.cpu().numpy()
     for u, t in enumerate(T):
@@ -221,8 +229,9 @@ def test_attention(K, H, nh):
     M = sum(T)
     qkv = (rng.standard_normal((M, 3 * H)) * 1.5).astype(np.float16)
     out = torch.zeros(M, H, device="cuda", dtype=torch.float16)
-    K.attention(torch.from_numpy(qkv).cuda().data_ptr(), out.data_ptr(), torch.from_numpy(off).cuda().data_ptr(),
-                torch.tensor(T, dtype=torch.int32).cuda().data_ptr(), len(T), H, nh, max(T), stream())
+    d_qkv, d_off, d_T = dev(qkv), dev(off), dev(np.array(T, np.int32))
+    K.attention(d_qkv.data_ptr(), out.data_ptr(), d_off.data_ptr(), d_T.data_ptr(), len(T), H, nh, max(T),
+                stream())
     torch.cuda.synchronize()
     got = out.float().cpu().numpy()
     d = H // nh
@@ -251,8 +260,8 @@ def test_ctc_greedy_bit_exact(K):
     ids = torch.zeros(M, dtype=torch.int32, device="cuda")
     spans = torch.zeros(3 * M, dtype=torch.int32, device="cuda")
     ns = torch.zeros(len(T), dtype=torch.int32, device="cuda")
-    K.ctc_greedy(d_lg.data_ptr(), torch.from_numpy(off).cuda().data_ptr(),
-                 torch.tensor(T, dtype=torch.int32).cuda().data_ptr(), len(T), V, ids.data_ptr(), spans.data_ptr(),
+    d_off, d_T = dev(off), dev(np.array(T, np.int32))
+    K.ctc_greedy(d_lg.data_ptr(), d_off.data_ptr(), d_T.data_ptr(), len(T), V, ids.data_ptr(), spans.data_ptr(),
                  ns.data_ptr(), max(T), stream())
     torch.cuda.synchronize()
     sp, n = spans.cpu().numpy(), ns.cpu().numpy()

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "engine.hpp"
+#include "shard.hpp"
 #include "wav2vec2_b200.h"
 
 using namespace w2v;
@@ -181,72 +182,34 @@ wav2vec2_result* make_result(const ModelConfig& c, int T, const std::string& tex
     return r;
 }
 
-// Batches of utterance indices: longest first, at most max_batch utterances
-// and a bounded number of samples per batch (length bucketing keeps padding
-// in the conv extractor small).
-std::vector<std::vector<int>> make_batches(const int* n_samples, int n_utt, int max_batch) {
-    std::vector<int> order(n_utt);
-    for (int i = 0; i < n_utt; i++) order[i] = i;
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return n_samples[a] > n_samples[b]; });
-    const long long budget = (long long)max_batch * 16000LL * 32;   // ~32 s per slot
-    std::vector<std::vector<int>> batches;
-    std::vector<int> cur;
-    long long cur_max = 0;
-    for (int i : order) {
-        const long long n = std::max(n_samples[i], 1);
-        const long long new_max = std::max(cur_max, n);
-        if (!cur.empty() && ((int)cur.size() >= max_batch || new_max * (long long)(cur.size() + 1) > budget)) {
-            batches.push_back(cur);
-            cur.clear();
-            cur_max = 0;
-        }
-        cur.push_back(i);
-        cur_max = std::max(cur_max, n);
-    }
-    if (!cur.empty()) batches.push_back(cur);
-    return batches;
-}
-
-// Run every batch, sharded over the context's devices (one host thread per
-// device pulling from a shared queue); fn(engine, batch index list, logits,
-// spans, n_spans, geometry) consumes each result on the worker thread.
+// Run every batch, sharded over the context's devices (shard.hpp: one host
+// thread per device pulling from a shared queue; a failing device retires and
+// its batch is re-queued); fn(engine, batch index list, logits, spans,
+// n_spans, geometry) consumes each result on the worker thread.
 template <typename Fn>
 void run_sharded(wav2vec2_context* ctx, const float* const* samples, const int* n_samples, int n_utt,
                  bool want_logits, bool want_spans, Fn fn) {
-    auto batches = make_batches(n_samples, n_utt, ctx->max_batch);
-    std::atomic<size_t> next{0};
-    std::mutex err_mu;
-    std::string first_err;
-    auto worker = [&](Engine* e) {
+    const auto batches = make_batches(n_samples, n_utt, ctx->max_batch, (long long)ctx->max_batch * 16000LL * 32);
+    const int nw = (int)std::min(ctx->engines.size(), std::max<size_t>(batches.size(), 1));
+    run_batches(batches.size(), nw, [&](int w, size_t bi, std::string& err) {
+        Engine* e = ctx->engines[w].get();
         std::vector<float> logits;
         std::vector<int> spans, nsp;
-        for (;;) {
-            const size_t bi = next.fetch_add(1);
-            if (bi >= batches.size()) break;
-            try {
-                const auto& b = batches[bi];
-                std::vector<const float*> a;
-                std::vector<int> ns;
-                for (int i : b) { a.push_back(samples[i]); ns.push_back(n_samples[i]); }
-                BatchGeom g;
-                e->run_host(a, ns, want_logits ? &logits : nullptr, want_spans ? &spans : nullptr,
-                            want_spans ? &nsp : nullptr, &g);
-                fn(e, b, logits, spans, nsp, g);
-            } catch (const std::exception& ex) {
-                std::lock_guard<std::mutex> lk(err_mu);
-                if (first_err.empty()) first_err = ex.what();
-                next.store(batches.size());
-            }
+        const auto& b = batches[bi];
+        std::vector<const float*> a;
+        std::vector<int> ns;
+        for (int i : b) { a.push_back(samples[i]); ns.push_back(n_samples[i]); }
+        BatchGeom g;
+        try {
+            e->run_host(a, ns, want_logits ? &logits : nullptr, want_spans ? &spans : nullptr,
+                        want_spans ? &nsp : nullptr, &g);
+        } catch (const std::exception& ex) {
+            err = std::string("device ") + std::to_string(e->device()) + ": " + ex.what();
+            return false;
         }
-    };
-    if (ctx->engines.size() == 1 || batches.size() <= 1) {
-        worker(ctx->engines[0].get());
-    } else {
-        std::vector<std::thread> th;
-        for (auto& e : ctx->engines) th.emplace_back(worker, e.get());
-        for (auto& t : th) t.join();
-    }
-    if (!first_err.empty()) throw std::runtime_error(first_err);
+        fn(e, b, logits, spans, nsp, g);
+        return true;
+    });
 }
 
 }  // namespace
@@ -474,7 +437,11 @@ int wav2vec2_b200_debug_stages(wav2vec2_context* ctx, const float* samples, int 
         if (g.M == 0) throw std::runtime_error("utterance too short");
         void* d = nullptr;
         if (cudaMalloc(&d, (size_t)n_samples * 4) != cudaSuccess) throw std::runtime_error("cudaMalloc");
-        cudaMemcpy(d, samples, (size_t)n_samples * 4, cudaMemcpyHostToDevice);
+        // same stream as the forward: a pageable cudaMemcpy may return before its DMA lands
+        if (cudaMemcpyAsync(d, samples, (size_t)n_samples * 4, cudaMemcpyHostToDevice, e->stream()) != cudaSuccess) {
+            cudaFree(d);
+            throw std::runtime_error("audio upload");
+        }
         e->forward(static_cast<float*>(d), g, e->stream(), feat, stages);
         if (logits)
             cudaMemcpyAsync(logits, e->d_logits(), (size_t)g.M * ctx->cfg.vocab * 4, cudaMemcpyDeviceToHost,

@@ -1,6 +1,7 @@
 #include "engine.hpp"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 
@@ -167,7 +168,10 @@ Engine::Engine(const GgufFile& gf, const ModelConfig& cfg, int device) : cfg_(cf
     cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
     cuda_check(cudaEventCreateWithFlags(&meta_done_, cudaEventDisableTiming), "cudaEventCreate");
     err_.ensure(sizeof(int));
-    cuda_check(cudaMemset(err_.p, 0, sizeof(int)), "cudaMemset");
+    // Every transfer of the engine is ordered on its own (non-blocking) stream:
+    // a legacy-stream cudaMemcpy from pageable memory may return before its DMA
+    // lands and is not ordered against this stream.
+    cuda_check(cudaMemsetAsync(err_.p, 0, sizeof(int), stream_), "cudaMemsetAsync");
     load(gf);
     cuda_check(cudaStreamSynchronize(stream_), "weight upload");
 }
@@ -193,9 +197,11 @@ Engine::~Engine() {
     if (stream_) cudaStreamDestroy(stream_);
 }
 
-static void upload_floats(DevBuf& d, const std::vector<float>& v) {
+// Pageable source: cudaMemcpyAsync stages the data before returning, so v may
+// be released right after; the copy itself is ordered on `st`.
+static void upload_floats(DevBuf& d, const std::vector<float>& v, cudaStream_t st) {
     d.ensure(v.size() * sizeof(float));
-    cuda_check(cudaMemcpy(d.p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice), "upload");
+    cuda_check(cudaMemcpyAsync(d.p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice, st), "upload");
 }
 
 static std::vector<float> floats_sized(const GgufFile& gf, const std::string& name, size_t n) {
@@ -207,7 +213,7 @@ static std::vector<float> floats_sized(const GgufFile& gf, const std::string& na
 // fp32 host data -> fp16 device buffer (via a temporary fp32 upload).
 static void upload_f16(DevBuf& d, const std::vector<float>& v, cudaStream_t st) {
     DevBuf tmp;
-    upload_floats(tmp, v);
+    upload_floats(tmp, v, st);
     d.ensure(v.size() * 2);
     w2v_check(w2v_dequant_f16(tmp.p, 0, 1, (long long)v.size(), d.p, st), "fp16 weight conversion");
     cuda_check(cudaStreamSynchronize(st), "fp16 weight conversion");
@@ -226,7 +232,7 @@ void Engine::upload_linear(const GgufFile& gf, const std::string& name, int N, i
         throw std::runtime_error("tensor size mismatch: " + name + ".weight");
     DevBuf raw;
     raw.ensure(t.nbytes);
-    cuda_check(cudaMemcpy(raw.p, t.data, t.nbytes, cudaMemcpyHostToDevice), "weight upload");
+    cuda_check(cudaMemcpyAsync(raw.p, t.data, t.nbytes, cudaMemcpyHostToDevice, stream_), "weight upload");
     w2v_check(w2v_dequant_f16(raw.p, (int)t.type, N, K, static_cast<uint16_t*>(w.p) + row_offset * K, stream_),
               "weight expansion");
     cuda_check(cudaStreamSynchronize(stream_), "weight expansion");
@@ -237,17 +243,17 @@ void Engine::load(const GgufFile& gf) {
     const ModelConfig& c = cfg_;
     const int C = c.conv_dim, H = c.hidden, F = c.ffn, V = c.vocab;
     // conv layer 0: [C][1][k0] fp32 (src/wav2vec2.cpp:182-202)
-    upload_floats(conv0_w_, floats_sized(gf, "feature_extractor.conv_layers.0.conv.weight", (size_t)C * c.conv_k[0]));
+    upload_floats(conv0_w_, floats_sized(gf, "feature_extractor.conv_layers.0.conv.weight", (size_t)C * c.conv_k[0]), stream_);
     conv_w_.resize(c.n_conv);
     conv_b_.resize(c.n_conv);
     conv_gw_.resize(c.n_conv);
     conv_gb_.resize(c.n_conv);
     for (int i = 0; i < c.n_conv; i++) {
         const std::string p = "feature_extractor.conv_layers." + std::to_string(i);
-        if (c.conv_bias[i]) upload_floats(conv_b_[i], floats_sized(gf, p + ".conv.bias", C));
+        if (c.conv_bias[i]) upload_floats(conv_b_[i], floats_sized(gf, p + ".conv.bias", C), stream_);
         if (c.conv_norm[i]) {
-            upload_floats(conv_gw_[i], floats_sized(gf, p + ".layer_norm.weight", C));
-            upload_floats(conv_gb_[i], floats_sized(gf, p + ".layer_norm.bias", C));
+            upload_floats(conv_gw_[i], floats_sized(gf, p + ".layer_norm.weight", C), stream_);
+            upload_floats(conv_gb_[i], floats_sized(gf, p + ".layer_norm.bias", C), stream_);
         }
         if (i == 0) continue;
         // [co][ci][k] -> implicit-GEMM B operand [co][k*C + ci]
@@ -260,11 +266,11 @@ void Engine::load(const GgufFile& gf) {
         upload_f16(conv_w_[i], r, stream_);
     }
     // feature projection (src/wav2vec2.cpp:205-208)
-    upload_floats(proj_lnw_, floats_sized(gf, "feature_projection.layer_norm.weight", C));
-    upload_floats(proj_lnb_, floats_sized(gf, "feature_projection.layer_norm.bias", C));
+    upload_floats(proj_lnw_, floats_sized(gf, "feature_projection.layer_norm.weight", C), stream_);
+    upload_floats(proj_lnb_, floats_sized(gf, "feature_projection.layer_norm.bias", C), stream_);
     proj_w_.ensure((size_t)H * C * 2);
     upload_linear(gf, "feature_projection.projection", H, C, proj_w_);
-    upload_floats(proj_b_, floats_sized(gf, "feature_projection.projection.bias", H));
+    upload_floats(proj_b_, floats_sized(gf, "feature_projection.projection.bias", H), stream_);
     // positional conv [H][Cg][Kp] -> [G][Kp][co][ci] (src/wav2vec2.cpp:211-212)
     {
         const int G = c.pos_g, Cg = H / G, Kp = c.pos_k;
@@ -276,10 +282,10 @@ void Engine::load(const GgufFile& gf) {
                     for (int k = 0; k < Kp; k++)
                         r[(((size_t)g * Kp + k) * Cg + oc) * Cg + ic] = w[((size_t)(g * Cg + oc) * Cg + ic) * Kp + k];
         upload_f16(pos_w_, r, stream_);
-        upload_floats(pos_b_, floats_sized(gf, "encoder.pos_conv_embed.conv.bias", H));
+        upload_floats(pos_b_, floats_sized(gf, "encoder.pos_conv_embed.conv.bias", H), stream_);
     }
-    upload_floats(enc_lnw_, floats_sized(gf, "encoder.layer_norm.weight", H));
-    upload_floats(enc_lnb_, floats_sized(gf, "encoder.layer_norm.bias", H));
+    upload_floats(enc_lnw_, floats_sized(gf, "encoder.layer_norm.weight", H), stream_);
+    upload_floats(enc_lnb_, floats_sized(gf, "encoder.layer_norm.bias", H), stream_);
     // encoder layers (src/wav2vec2.cpp:219-242); Q, K, V stacked into one [3H, H]
     layers_.resize(c.n_layers);
     for (int l = 0; l < c.n_layers; l++) {
@@ -294,25 +300,25 @@ void Engine::load(const GgufFile& gf) {
         auto bv = floats_sized(gf, p + ".attention.v_proj.bias", H);
         bq.insert(bq.end(), bk.begin(), bk.end());
         bq.insert(bq.end(), bv.begin(), bv.end());
-        upload_floats(L.bqkv, bq);
+        upload_floats(L.bqkv, bq, stream_);
         L.wo.ensure((size_t)H * H * 2);
         upload_linear(gf, p + ".attention.out_proj", H, H, L.wo);
-        upload_floats(L.bo, floats_sized(gf, p + ".attention.out_proj.bias", H));
+        upload_floats(L.bo, floats_sized(gf, p + ".attention.out_proj.bias", H), stream_);
         L.w1.ensure((size_t)F * H * 2);
         upload_linear(gf, p + ".feed_forward.intermediate_dense", F, H, L.w1);
-        upload_floats(L.b1, floats_sized(gf, p + ".feed_forward.intermediate_dense.bias", F));
+        upload_floats(L.b1, floats_sized(gf, p + ".feed_forward.intermediate_dense.bias", F), stream_);
         L.w2.ensure((size_t)H * F * 2);
         upload_linear(gf, p + ".feed_forward.output_dense", H, F, L.w2);
-        upload_floats(L.b2, floats_sized(gf, p + ".feed_forward.output_dense.bias", H));
-        upload_floats(L.ln1w, floats_sized(gf, p + ".layer_norm.weight", H));
-        upload_floats(L.ln1b, floats_sized(gf, p + ".layer_norm.bias", H));
-        upload_floats(L.ln2w, floats_sized(gf, p + ".final_layer_norm.weight", H));
-        upload_floats(L.ln2b, floats_sized(gf, p + ".final_layer_norm.bias", H));
+        upload_floats(L.b2, floats_sized(gf, p + ".feed_forward.output_dense.bias", H), stream_);
+        upload_floats(L.ln1w, floats_sized(gf, p + ".layer_norm.weight", H), stream_);
+        upload_floats(L.ln1b, floats_sized(gf, p + ".layer_norm.bias", H), stream_);
+        upload_floats(L.ln2w, floats_sized(gf, p + ".final_layer_norm.weight", H), stream_);
+        upload_floats(L.ln2b, floats_sized(gf, p + ".final_layer_norm.bias", H), stream_);
     }
     // CTC head (src/wav2vec2.cpp:245-246)
     lm_w_.ensure((size_t)V * H * 2);
     upload_linear(gf, "lm_head", V, H, lm_w_);
-    upload_floats(lm_b_, floats_sized(gf, "lm_head.bias", V));
+    upload_floats(lm_b_, floats_sized(gf, "lm_head.bias", V), stream_);
 }
 
 // ── per-batch geometry and workspace ────────────────────────────────────────
@@ -410,8 +416,13 @@ void Engine::upload_meta(const BatchGeom& g, cudaStream_t st) {
 int Engine::check_device_error() {
     int e = 0;
     cudaSetDevice(device_);
-    if (cudaMemcpy(&e, err_.p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
-    if (e) cudaMemset(err_.p, 0, sizeof(int));
+    if (cudaMemcpyAsync(&e, err_.p, sizeof(int), cudaMemcpyDeviceToHost, stream_) != cudaSuccess ||
+        cudaStreamSynchronize(stream_) != cudaSuccess)
+        return -1;
+    if (e) {
+        cudaMemsetAsync(err_.p, 0, sizeof(int), stream_);
+        cudaStreamSynchronize(stream_);
+    }
     return e;
 }
 

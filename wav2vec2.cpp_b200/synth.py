@@ -282,6 +282,8 @@ def cached_model(dirpath: str | Path, arch: str, dtype: str, seed: int = 0, **kw
 def make_audio(n_samples: int, seed: int, sr: int = 16000) -> np.ndarray:
     """Seeded synthetic utterance: 5 sinusoids + N(0, 0.05^2) noise, peak 0.9, float32."""
     rng = np.random.default_rng(seed)
+    if n_samples <= 0:
+        return np.zeros(0, np.float32)
     f = rng.uniform(80.0, 4000.0, 5)
     ph = rng.uniform(0.0, 2 * np.pi, 5)
     amp = rng.uniform(0.1, 1.0, 5)
