@@ -26,6 +26,7 @@ enum {
     W2V_ERR_DRIVER = 3,      /* driver entry point unavailable */
     W2V_ERR_TENSOR_MAP = 4,  /* cuTensorMapEncodeTiled rejected the view */
     W2V_ERR_DEVICE = 5,      /* kernel reported a device-side error */
+    W2V_ERR_CAPACITY = 6,    /* request exceeds a fixed, built-in buffer */
 };
 
 /* GEMM epilogues. */
@@ -79,6 +80,21 @@ int w2v_conv0(const float* audio, const long long* off, const int* len, const in
               const float* stats, const float* w0, const float* b0, int C, int k0, int s0, int norm,
               const float* gw, const float* gb, double* gn_sums, void* out, long long rows_max,
               int max_frames, void* stream);
+
+/* w2v_conv0 for callers that cannot allocate device memory.  No counterpart
+ * in the reference (which has no GPU code): same arguments and result as
+ * w2v_conv0 without gn_sums; the GroupNorm statistics live in a 512 KiB
+ * buffer inside the library, per device, held until process exit.
+ *   Limit: with norm == 1, n_utt <= 64 and C <= 512, else W2V_ERR_CAPACITY
+ *   (and nothing is launched).
+ *   It calls no cudaMalloc/cudaFree.  The first call on a device looks the
+ *   buffer's device address up once (make that first call before any stream
+ *   capture).  All calls on a device share the buffer: calls that overlap on
+ *   the GPU (different streams, no ordering) race on it. */
+int w2v_conv0_noalloc(const float* audio, const long long* off, const int* len, const int* frames,
+                      int n_utt, const float* stats, const float* w0, const float* b0, int C, int k0,
+                      int s0, int norm, const float* gw, const float* gb, void* out, long long rows_max,
+                      int max_frames, void* stream);
 
 /* Row LayerNorm (eps 1e-5, src/ops.h:24-36) over D columns of fp16 or fp32
  * rows, optional GELU after the affine, fp32 and/or fp16 outputs.

@@ -61,6 +61,8 @@ SIGNATURES = {
     "w2v_wave_stats": (_i, [_vp, _vp, _vp, _i, _vp, _vp]),
     "w2v_conv0": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _ll, _i,
                        _vp]),
+    "w2v_conv0_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _ll, _i,
+                               _vp]),
     "w2v_layer_norm": (_i, [_vp, _i, _ll, _ll, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _ll, _vp]),
     "w2v_pos_conv": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp]),
     "w2v_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),

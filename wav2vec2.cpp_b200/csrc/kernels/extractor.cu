@@ -1,6 +1,8 @@
 // Bandwidth-bound kernels around the GEMMs: weight expansion at load time,
 // waveform statistics, conv layer 0 with its norm + GELU, row LayerNorm and
 // the greedy CTC decoder.
+#include <mutex>
+
 #include "common.cuh"
 #include "w2v_kernels.h"
 
@@ -409,4 +411,53 @@ extern "C" int w2v_ctc_greedy(const float* logits, const long long* off, const i
     (void)max_T;
     ctc_greedy_kernel<<<n_utt, 256, 0, S(stream)>>>(logits, off, T, V, ids, spans, n_spans);
     return launch_rc();
+}
+
+// ── conv layer 0 for callers that cannot allocate device memory ─────────────
+// Some hosts cannot call cudaMalloc once they are running: e.g. a process
+// whose device memory is owned by another allocator, or a real-time audio
+// thread that must not make a call that can block on the device.  For those
+// callers this variant of w2v_conv0 keeps the GroupNorm statistics (its only
+// scratch memory) in a fixed buffer compiled into this library instead of a
+// caller-provided one.  The buffer is a file-scope __device__ array: every GPU
+// that loads the library holds it (512 KiB) until the process exits.
+namespace {
+constexpr int kNoAllocMaxUtt = 64;        // utterances per call (GroupNorm models)
+constexpr int kNoAllocMaxChannels = 512;  // conv channels
+constexpr int kNoAllocMaxDevices = 64;
+__device__ __align__(256) double g_conv0_gn_scratch[kNoAllocMaxUtt * kNoAllocMaxChannels * 2];
+
+std::mutex g_scratch_mu;
+double* g_scratch_addr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address is looked up
+// once per device (with that device current) and cached.
+int scratch_address(double** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return W2V_ERR_LAUNCH;
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_conv0_gn_scratch) != cudaSuccess || !p) return W2V_ERR_LAUNCH;
+        g_scratch_addr[dev] = static_cast<double*>(p);
+    }
+    *out = g_scratch_addr[dev];
+    return W2V_OK;
+}
+}  // namespace
+
+extern "C" int w2v_conv0_noalloc(const float* audio, const long long* off, const int* len, const int* frames,
+                                 int n_utt, const float* stats, const float* w0, const float* b0, int C, int k0,
+                                 int s0, int norm, const float* gw, const float* gb, void* out, long long rows_max,
+                                 int max_frames, void* stream) {
+    double* gn = nullptr;
+    if (norm == 1) {
+        if (n_utt > kNoAllocMaxUtt || C > kNoAllocMaxChannels) return W2V_ERR_CAPACITY;
+        const int rc = scratch_address(&gn);
+        if (rc != W2V_OK) return rc;
+    }
+    // w2v_conv0 zeroes the statistics before accumulating into them.
+    return w2v_conv0(audio, off, len, frames, n_utt, stats, w0, b0, C, k0, s0, norm, gw, gb, gn, out, rows_max,
+                     max_frames, stream);
 }
