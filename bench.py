@@ -324,6 +324,59 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_kernel_case(args):
+    """One kernel at a representative size (for ncu captures and micro-timing):
+    gemm: encoder fc1 shape (M rows x K=768 -> N=3072, fp16 out, GELU epilogue);
+    attention: 64 utterances x 499 frames, 12 heads x 64;
+    pos_conv: the same batch, hidden 768, kernel 128, 16 groups."""
+    import torch
+    pkg()
+    import w2v_b200.binding as b
+    K = b.kernels
+    torch.manual_seed(0)
+    st = torch.cuda.current_stream().cuda_stream
+    M = args.rows
+    if args.kernel == "gemm":
+        Kd, N = 768, 3072
+        A = torch.randn(M, Kd, device="cuda").half()
+        W = (torch.randn(N, Kd, device="cuda") * 0.05).half()
+        bias = torch.randn(N, device="cuda")
+        out = torch.empty(M, N, device="cuda", dtype=torch.float16)
+        fn = lambda: K.gemm(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, out.data_ptr(), N, M, M,
+                            bias.data_ptr(), 0, N, 1, 0, 0, st)
+        flops = 2.0 * M * N * Kd
+    elif args.kernel == "attention":
+        H, nh, T, B = 768, 12, 499, 64
+        qkv = torch.randn(B * T, 3 * H, device="cuda").half()
+        out = torch.empty(B * T, H, device="cuda", dtype=torch.float16)
+        off = torch.arange(B, device="cuda", dtype=torch.int64) * T
+        Tt = torch.full((B,), T, device="cuda", dtype=torch.int32)
+        fn = lambda: K.attention(qkv.data_ptr(), out.data_ptr(), off.data_ptr(), Tt.data_ptr(), B, H, nh, T, st)
+        flops = 4.0 * B * T * T * H
+    else:
+        H, G, Kp, T, B = 768, 16, 128, 499, 64
+        x = torch.randn(B * T, H, device="cuda")
+        out = torch.empty_like(x)
+        wt = (torch.randn(G, Kp, H // G, H // G, device="cuda") * 0.02).half()
+        bias = torch.randn(H, device="cuda")
+        off = torch.arange(B, device="cuda", dtype=torch.int64) * T
+        Tt = torch.full((B,), T, device="cuda", dtype=torch.int32)
+        fn = lambda: K.pos_conv(out.data_ptr(), x.data_ptr(), off.data_ptr(), Tt.data_ptr(), B, H, Kp, G,
+                                wt.data_ptr(), bias.data_ptr(), T, st)
+        flops = 2.0 * B * T * Kp * (H // G) * H
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"kernel": args.kernel, "rows": M, "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -339,7 +392,13 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for cpu_baseline")
     ap.add_argument("--ref-budget", type=float, default=150.0, help="seconds for the whole --impl reference run")
     ap.add_argument("--cache", default=os.environ.get("W2V_MODEL_CACHE", "/tmp/w2v_models"))
+    ap.add_argument("--kernel", choices=["gemm", "attention", "pos_conv"], default=None,
+                    help="time one kernel at a representative size instead of the whole step")
+    ap.add_argument("--rows", type=int, default=32768, help="GEMM rows for --kernel gemm")
     args = ap.parse_args()
+    if args.kernel:
+        run_kernel_case(args)
+        return
     args.world = int(os.environ.get("WORLD_SIZE", args.gpus))
     if args.impl == "reference":
         run_reference(args)

@@ -56,6 +56,12 @@ int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_stride, long 
                  const float* resid, long long ldr, int epilogue, int block_n, int* err,
                  void* stream);
 
+/* Failure-detection self-test: launches a kernel whose bounded mbarrier wait
+ * (the same wait the GEMM pipeline uses) is never satisfied; after limit_ms
+ * (1..2000) it writes the timeout code (1) to *err and returns without
+ * trapping, so the context stays usable.  No counterpart in the reference. */
+int w2v_selftest_wait_timeout(int* err, int limit_ms, void* stream);
+
 /* Expand GGUF linear weight rows ([N, K], GGUF type F32=0, F16=1, Q4_0=2,
  * Q8_0=8, raw bytes as stored in the file) to fp16 [N, K].  Block formats as
  * written by scripts/convert_to_gguf.py:63-97. */

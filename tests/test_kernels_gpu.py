@@ -269,3 +269,22 @@ def test_ctc_greedy_bit_exact(K):
         ref = O.greedy_spans(lg[off[u]:off[u] + t])
         got = [tuple(int(v) for v in sp[3 * (off[u] + i): 3 * (off[u] + i) + 3]) for i in range(n[u])]
         assert got == ref
+
+
+def test_bounded_wait_expires_and_context_survives(K):
+    """A wait that can never be satisfied ends with an error status (no hang,
+    no trap), and the context keeps working afterwards."""
+    import w2v_b200.binding as b
+    err = err_word()
+    assert b.lib().w2v_selftest_wait_timeout(err.data_ptr(), 50, stream()) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1                    # kErrBarrierTimeout
+    A = torch.randn(128, 64, device="cuda").half()
+    W = torch.randn(64, 64, device="cuda").half()
+    out = torch.empty(128, 64, device="cuda")
+    err2 = err_word()
+    K.gemm(A.data_ptr(), 64, 1, 1, 64, 128, 1, 128 * 64, W.data_ptr(), 64, out.data_ptr(), 64, 128, 128,
+           epilogue=EPI_F32, err=err2.data_ptr(), stream=stream())
+    torch.cuda.synchronize()
+    assert int(err2.item()) == 0
+    assert torch.allclose(out, A.float() @ W.float().T, atol=1e-3, rtol=1e-3)

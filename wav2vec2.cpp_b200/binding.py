@@ -57,6 +57,7 @@ SIGNATURES = {
     # kernel layer (include/w2v_kernels.h)
     "w2v_gemm_f16": (_i, [_vp, _ll, _i, _i, _ll, _ll, _ll, _ll, _vp, _i, _vp, _ll, _ll, _i, _vp, _vp, _ll, _i,
                           _i, _vp, _vp]),
+    "w2v_selftest_wait_timeout": (_i, [_vp, _i, _vp]),
     "w2v_dequant_f16": (_i, [_vp, _i, _ll, _ll, _vp, _vp]),
     "w2v_wave_stats": (_i, [_vp, _vp, _vp, _i, _vp, _vp]),
     "w2v_conv0": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _ll, _i,

@@ -66,17 +66,20 @@ W2V_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait for the phase with the given parity.  Returns false (and
 // records the error) if the limit expired.
-W2V_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+W2V_DEV bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     uint32_t spins = 0;
     while (!mbar_try_wait(bar, parity)) {
-        if ((++spins & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+        if ((++spins & 255u) == 0 && globaltimer() - t0 > limit_ns) {
             report_error(err, kErrBarrierTimeout);
             return false;
         }
     }
     return true;
+}
+W2V_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+    return mbar_wait_for(bar, parity, err, kWaitLimitNs);
 }
 
 // ── TMA ────────────────────────────────────────────────────────────────────
@@ -193,11 +196,15 @@ W2V_DEV bool elect_one() {
 }
 
 // ── numerics ────────────────────────────────────────────────────────────────
-// tanh-approximation GELU exactly as the reference writes it (ops.h:18-21),
-// evaluated with the accurate tanhf.
+// The reference's tanh-approximation GELU (ops.h:18-21),
+//   0.5 x (1 + tanh(u)),  u = 0.7978845608 (x + 0.044715 x^3),
+// evaluated through the identity 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)):
+// one exp2 and one reciprocal on the special-function unit, relative error
+// ~1e-6 (well below the fp16 rounding of every output it feeds).  Limits:
+// x -> -inf gives -0 (exp overflows to inf), x -> +inf gives x.
 W2V_DEV float gelu_tanh(float x) {
-    const float c = 0.7978845608028654f;
-    return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+    const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+    return __fdividef(x, 1.0f + __expf(-2.0f * u));
 }
 
 W2V_DEV uint32_t pack_half2(float a, float b) {

@@ -86,10 +86,14 @@ __global__ void wave_stats_kernel(const float* __restrict__ audio, const long lo
 }
 
 // ── conv layer 0 + norm + GELU (src/wav2vec2.cpp:273-287) ────────────────────
-// Block: 256 threads, each owning channels (2t, 2t+1) of C = 512 (C <= 512,
-// even); kFrames output frames per block.  The normalised samples the block
-// needs are staged in shared memory.
-constexpr int kC0Frames = 32;
+// Block: 256 threads, thread t owns channels (2t, 2t+1) (C <= 512, even) and
+// keeps their K0 taps in registers; the normalised samples the block needs
+// are staged once in shared memory and read as broadcasts.  Frames are
+// processed in register groups of 32.  K0 is 10 for every published model;
+// other first-layer kernels (<= 16) run the K0 = 16 instance with zero taps.
+constexpr int kC0Group = 32;        // frames per register group
+constexpr int kC0ApplyFrames = 256; // frames per apply block
+constexpr int kC0StatFrames = 1024; // frames per statistics block
 constexpr int kC0MaxK = 16;
 
 struct Conv0Args {
@@ -98,123 +102,166 @@ struct Conv0Args {
     const float* gw; const float* gb; double* gn; __half* out; long long rows_max;
 };
 
-W2V_DEV void conv0_compute(const Conv0Args& a, const float* xs, int f, int c, float& y0, float& y1,
-                           const float* w_s) {
-    float s0 = a.b0 ? __ldg(a.b0 + c) : 0.f, s1 = a.b0 ? __ldg(a.b0 + c + 1) : 0.f;
-    const float* x = xs + f * a.s0;
-    for (int k = 0; k < a.k0; k++) {
-        s0 += x[k] * w_s[c * a.k0 + k];
-        s1 += x[k] * w_s[(c + 1) * a.k0 + k];
-    }
-    y0 = s0; y1 = s1;
-}
-
-// stats pass (GroupNorm only): per-channel sum and sum of squares over frames.
-__global__ void conv0_gn_stats_kernel(Conv0Args a, int frames_per_block) {
-    extern __shared__ float sh[];
-    float* w_s = sh;                                  // [C][k0]
-    float* xs = sh + a.C * a.k0;                      // samples
-    const int u = blockIdx.y;
-    const int F = a.frames[u];
-    const int f0 = blockIdx.x * frames_per_block;
-    if (f0 >= F) return;
-    const int nf = min(frames_per_block, F - f0);
-    for (int i = threadIdx.x; i < a.C * a.k0; i += blockDim.x) w_s[i] = a.w0[i];
+// Stage normalised samples for frames f0 .. f0+nf-1 (zero-padded by kC0MaxK).
+W2V_DEV void conv0_stage(const Conv0Args& a, int u, int f0, int nf, float* xs) {
     const float mean = a.stats[2 * u], inv = a.stats[2 * u + 1];
     const float* x = a.audio + a.off[u];
     const int ns = (nf - 1) * a.s0 + a.k0;
-    for (int i = threadIdx.x; i < ns; i += blockDim.x) xs[i] = (x[f0 * a.s0 + i] - mean) * inv;
+    for (int i = threadIdx.x; i < ns + kC0MaxK; i += blockDim.x)
+        xs[i] = i < ns ? (x[(long long)f0 * a.s0 + i] - mean) * inv : 0.f;
+}
+
+template <int K0>
+W2V_DEV void conv0_load_w(const Conv0Args& a, int c, float (&w)[2][K0], float& b0, float& b1) {
+#pragma unroll
+    for (int k = 0; k < K0; k++) {
+        w[0][k] = k < a.k0 ? __ldg(a.w0 + c * a.k0 + k) : 0.f;
+        w[1][k] = k < a.k0 ? __ldg(a.w0 + (c + 1) * a.k0 + k) : 0.f;
+    }
+    b0 = a.b0 ? __ldg(a.b0 + c) : 0.f;
+    b1 = a.b0 ? __ldg(a.b0 + c + 1) : 0.f;
+}
+
+template <int K0>
+W2V_DEV void conv0_group(const float* xs, int g0, int s0, const float (&w)[2][K0], float b0, float b1,
+                         float (&y)[kC0Group][2]) {
+#pragma unroll
+    for (int f = 0; f < kC0Group; f++) {
+        const float* x = xs + (g0 + f) * s0;
+        float y0 = b0, y1 = b1;
+#pragma unroll
+        for (int k = 0; k < K0; k++) {
+            const float v = x[k];
+            y0 = fmaf(v, w[0][k], y0);
+            y1 = fmaf(v, w[1][k], y1);
+        }
+        y[f][0] = y0;
+        y[f][1] = y1;
+    }
+}
+
+// Statistics pass (GroupNorm only): per-channel sum and sum of squares over
+// the utterance's frames, accumulated in fp64.
+template <int K0>
+__global__ void __launch_bounds__(256) conv0_gn_stats_kernel(Conv0Args a) {
+    extern __shared__ float xs[];
+    const int u = blockIdx.y;
+    const int F = a.frames[u];
+    const int f0 = blockIdx.x * kC0StatFrames;
+    if (f0 >= F) return;
+    const int nf = min(kC0StatFrames, F - f0);
+    conv0_stage(a, u, f0, nf, xs);
     __syncthreads();
     const int c = 2 * threadIdx.x;
     if (c >= a.C) return;
+    float w[2][K0], b0, b1;
+    conv0_load_w<K0>(a, c, w, b0, b1);
     double s0 = 0, s1 = 0, q0 = 0, q1 = 0;
-    for (int f = 0; f < nf; f++) {
-        float y0, y1;
-        conv0_compute(a, xs, f, c, y0, y1, w_s);
-        s0 += y0; s1 += y1; q0 += (double)y0 * y0; q1 += (double)y1 * y1;
+    for (int g0 = 0; g0 < nf; g0 += kC0Group) {
+        float y[kC0Group][2];
+        conv0_group<K0>(xs, g0, a.s0, w, b0, b1, y);
+        float ps0 = 0.f, ps1 = 0.f, pq0 = 0.f, pq1 = 0.f;   // fp32 within a group of <= 32 frames
+#pragma unroll
+        for (int f = 0; f < kC0Group; f++) {
+            if (g0 + f < nf) {
+                ps0 += y[f][0]; ps1 += y[f][1];
+                pq0 = fmaf(y[f][0], y[f][0], pq0); pq1 = fmaf(y[f][1], y[f][1], pq1);
+            }
+        }
+        s0 += ps0; s1 += ps1; q0 += pq0; q1 += pq1;
     }
     double* g = a.gn + ((long long)u * a.C + c) * 2;
     atomicAdd(g + 0, s0); atomicAdd(g + 1, q0);
     atomicAdd(g + 2, s1); atomicAdd(g + 3, q1);
 }
 
-__global__ void conv0_apply_kernel(Conv0Args a) {
-    extern __shared__ float sh[];
-    float* w_s = sh;
-    float* xs = sh + a.C * a.k0;
-    __shared__ float red[8][kC0Frames];
-    __shared__ float rowstat[2][kC0Frames];
+template <int K0>
+__global__ void __launch_bounds__(256) conv0_apply_kernel(Conv0Args a) {
+    extern __shared__ float xs[];
+    __shared__ float red[8][kC0Group];
+    __shared__ float rowstat[2][kC0Group];
     const int u = blockIdx.y;
     const int F = a.frames[u];
-    const int f0 = blockIdx.x * kC0Frames;
+    const int f0 = blockIdx.x * kC0ApplyFrames;
     if (f0 >= F) return;
-    const int nf = min(kC0Frames, F - f0);
-    for (int i = threadIdx.x; i < a.C * a.k0; i += blockDim.x) w_s[i] = a.w0[i];
-    const float mean = a.stats[2 * u], inv = a.stats[2 * u + 1];
-    const float* x = a.audio + a.off[u];
-    const int ns = (nf - 1) * a.s0 + a.k0;
-    for (int i = threadIdx.x; i < ns; i += blockDim.x) xs[i] = (x[f0 * a.s0 + i] - mean) * inv;
+    const int nf = min(kC0ApplyFrames, F - f0);
+    conv0_stage(a, u, f0, nf, xs);
     __syncthreads();
     const int c = 2 * threadIdx.x;
     const bool active = c < a.C;
-    float y[kC0Frames][2];
-#pragma unroll
-    for (int f = 0; f < kC0Frames; f++) {
-        y[f][0] = y[f][1] = 0.f;
-        if (active && f < nf) conv0_compute(a, xs, f, c, y[f][0], y[f][1], w_s);
-    }
-    if (a.norm == 1 && active) {
-        // GroupNorm (one group per channel) over all frames of the utterance
-        // (src/ops.h:39-50); statistics from the stats pass.
-        const double* g = a.gn + ((long long)u * a.C + c) * 2;
-        float m[2], iv[2];
-        for (int j = 0; j < 2; j++) {
-            const double mu = g[2 * j] / F;
-            const float var = (float)fmax(g[2 * j + 1] / F - mu * mu, 0.0);
-            m[j] = (float)mu;
-            iv[j] = 1.f / sqrtf(var + 1e-5f);
+    float w[2][K0], b0 = 0.f, b1 = 0.f;
+    float m[2] = {0.f, 0.f}, iv[2] = {1.f, 1.f}, ga[2] = {1.f, 1.f}, be[2] = {0.f, 0.f};
+    if (active) {
+        conv0_load_w<K0>(a, c, w, b0, b1);
+        if (a.norm) {
+            ga[0] = a.gw[c]; ga[1] = a.gw[c + 1];
+            be[0] = a.gb[c]; be[1] = a.gb[c + 1];
         }
+        if (a.norm == 1) {
+            // GroupNorm (one group per channel) over all frames of the
+            // utterance (src/ops.h:39-50), statistics from the stats pass
+            const double* g = a.gn + ((long long)u * a.C + c) * 2;
 #pragma unroll
-        for (int f = 0; f < kC0Frames; f++)
-            for (int j = 0; j < 2; j++) y[f][j] = (y[f][j] - m[j]) * iv[j] * a.gw[c + j] + a.gb[c + j];
-    } else if (a.norm == 2) {
-        // LayerNorm over channels per frame (src/ops.h:24-36), two-pass.
-        const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-        for (int pass = 0; pass < 2; pass++) {
+            for (int j = 0; j < 2; j++) {
+                const double mu = g[2 * j] / F;
+                const float var = (float)fmax(g[2 * j + 1] / F - mu * mu, 0.0);
+                m[j] = (float)mu;
+                iv[j] = 1.f / sqrtf(var + 1e-5f);
+            }
+        }
+    } else {
 #pragma unroll
-            for (int f = 0; f < kC0Frames; f++) {
-                float v = 0.f;
-                if (active) {
-                    if (pass == 0) v = y[f][0] + y[f][1];
-                    else { const float d0 = y[f][0] - rowstat[0][f], d1 = y[f][1] - rowstat[0][f]; v = d0 * d0 + d1 * d1; }
+        for (int k = 0; k < K0; k++) w[0][k] = w[1][k] = 0.f;
+    }
+    const int wi = threadIdx.x >> 5, l = threadIdx.x & 31;
+    for (int g0 = 0; g0 < nf; g0 += kC0Group) {
+        float y[kC0Group][2];
+        conv0_group<K0>(xs, g0, a.s0, w, b0, b1, y);
+        if (a.norm == 2) {
+            // LayerNorm over channels per frame (src/ops.h:24-36), two-pass
+            for (int pass = 0; pass < 2; pass++) {
+#pragma unroll
+                for (int f = 0; f < kC0Group; f++) {
+                    float v = 0.f;
+                    if (active) {
+                        if (pass == 0) v = y[f][0] + y[f][1];
+                        else {
+                            const float d0 = y[f][0] - rowstat[0][f], d1 = y[f][1] - rowstat[0][f];
+                            v = d0 * d0 + d1 * d1;
+                        }
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (l == 0) red[wi][f] = v;
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (l == 0) red[w][f] = v;
+                __syncthreads();
+                if (threadIdx.x < kC0Group) {
+                    float sum = 0.f;
+                    for (int i = 0; i < (int)(blockDim.x >> 5); i++) sum += red[i][threadIdx.x];
+                    if (pass == 0) rowstat[0][threadIdx.x] = sum / a.C;
+                    else rowstat[1][threadIdx.x] = 1.f / sqrtf(sum / a.C + 1e-5f);
+                }
+                __syncthreads();
             }
-            __syncthreads();
-            if (threadIdx.x < kC0Frames) {
-                float s = 0.f;
-                for (int i = 0; i < (int)(blockDim.x >> 5); i++) s += red[i][threadIdx.x];
-                if (pass == 0) rowstat[0][threadIdx.x] = s / a.C;
-                else rowstat[1][threadIdx.x] = 1.f / sqrtf(s / a.C + 1e-5f);
-            }
-            __syncthreads();
         }
         if (active) {
 #pragma unroll
-            for (int f = 0; f < kC0Frames; f++)
-                for (int j = 0; j < 2; j++)
-                    y[f][j] = (y[f][j] - rowstat[0][f]) * rowstat[1][f] * a.gw[c + j] + a.gb[c + j];
+            for (int f = 0; f < kC0Group; f++) {
+                if (g0 + f < nf) {
+                    float v0 = y[f][0], v1 = y[f][1];
+                    if (a.norm == 1) {
+                        v0 = (v0 - m[0]) * iv[0] * ga[0] + be[0];
+                        v1 = (v1 - m[1]) * iv[1] * ga[1] + be[1];
+                    } else if (a.norm == 2) {
+                        v0 = (v0 - rowstat[0][f]) * rowstat[1][f] * ga[0] + be[0];
+                        v1 = (v1 - rowstat[0][f]) * rowstat[1][f] * ga[1] + be[1];
+                    }
+                    *reinterpret_cast<__half2*>(a.out + ((long long)u * a.rows_max + f0 + g0 + f) * a.C + c) =
+                        __floats2half2_rn(gelu_tanh(v0), gelu_tanh(v1));
+                }
+            }
         }
-    }
-    if (!active) return;
-#pragma unroll
-    for (int f = 0; f < kC0Frames; f++) {
-        if (f < nf) {
-            __half2 h = __floats2half2_rn(gelu_tanh(y[f][0]), gelu_tanh(y[f][1]));
-            *reinterpret_cast<__half2*>(a.out + ((long long)u * a.rows_max + f0 + f) * a.C + c) = h;
-        }
+        if (a.norm == 2) __syncthreads();   // rowstat is rewritten by the next group
     }
 }
 
@@ -264,6 +311,71 @@ __global__ void layer_norm_kernel(const void* __restrict__ in, int in_f16, long 
             if (gelu) y = gelu_tanh(y);
             if (out32) out32[orow * ld_out + col] = y;
             if (out16) out16[orow * ld_out + col] = __float2half_rn(y);
+        }
+    }
+}
+
+// Vectorised row LayerNorm: warp per row, each lane holds NV groups of 4
+// consecutive columns (D = 128 * NV); 16-byte fp32 / 8-byte fp16 accesses.
+template <int NV>
+__global__ void __launch_bounds__(256)
+layer_norm_vec_kernel(const void* __restrict__ in, int in_f16, long long ld_in, long long in_batch_rows,
+                      const int* __restrict__ rows, const long long* __restrict__ out_off, int n_batch, int n_rows,
+                      const float* __restrict__ w, const float* __restrict__ b, int gelu, float* __restrict__ out32,
+                      __half* __restrict__ out16, long long ld_out) {
+    constexpr int D = 128 * NV;
+    const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const long long rows_per_b = rows ? in_batch_rows : n_rows;
+    const long long bi = gw / rows_per_b, r = gw % rows_per_b;
+    if (bi >= n_batch) return;
+    if (r >= (rows ? rows[bi] : n_rows)) return;
+    const long long irow = bi * in_batch_rows + r;
+    const long long orow = out_off ? out_off[bi] + r : irow;
+    float v[NV][4];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        const int col = 4 * (lane + 32 * i);
+        if (in_f16) {
+            const uint2 p = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(in) + irow * ld_in + col);
+            const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&p.x));
+            const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&p.y));
+            v[i][0] = lo.x; v[i][1] = lo.y; v[i][2] = hi.x; v[i][3] = hi.y;
+        } else {
+            const float4 p = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in) + irow * ld_in + col);
+            v[i][0] = p.x; v[i][1] = p.y; v[i][2] = p.z; v[i][3] = p.w;
+        }
+        s += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / D;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) { const float d = v[i][j] - mean; q = fmaf(d, d, q); }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float inv = 1.f / sqrtf(q / D + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        const int col = 4 * (lane + 32 * i);
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(w + col));
+        const float4 bv = __ldg(reinterpret_cast<const float4*>(b + col));
+        float y[4] = {(v[i][0] - mean) * inv * wv.x + bv.x, (v[i][1] - mean) * inv * wv.y + bv.y,
+                      (v[i][2] - mean) * inv * wv.z + bv.z, (v[i][3] - mean) * inv * wv.w + bv.w};
+        if (gelu) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) y[j] = gelu_tanh(y[j]);
+        }
+        if (out32) *reinterpret_cast<float4*>(out32 + orow * ld_out + col) = make_float4(y[0], y[1], y[2], y[3]);
+        if (out16) {
+            uint2 p;
+            p.x = pack_half2(y[0], y[1]);
+            p.y = pack_half2(y[2], y[3]);
+            *reinterpret_cast<uint2*>(out16 + orow * ld_out + col) = p;
         }
     }
 }
@@ -368,18 +480,21 @@ extern "C" int w2v_conv0(const float* audio, const long long* off, const int* le
     if ((norm == 1 && !gn_sums) || (norm && (!gw || !gb))) return W2V_ERR_ARGS;
     if (n_utt <= 0 || max_frames <= 0) return W2V_OK;
     Conv0Args a{audio, off, len, frames, stats, w0, b0, C, k0, s0, norm, gw, gb, gn_sums, (__half*)out, rows_max};
+    const bool k10 = k0 == 10;
     if (norm == 1) {
-        cudaMemsetAsync(gn_sums, 0, sizeof(double) * 2 * C * (size_t)n_utt, S(stream));
-        const int fpb = 512;
-        const size_t sh = (size_t)(C * k0 + (fpb - 1) * s0 + k0) * sizeof(float);
-        dim3 g((max_frames + fpb - 1) / fpb, n_utt);
-        conv0_gn_stats_kernel<<<g, 256, sh, S(stream)>>>(a, fpb);
+        if (cudaMemsetAsync(gn_sums, 0, sizeof(double) * 2 * C * (size_t)n_utt, S(stream)) != cudaSuccess)
+            return W2V_ERR_LAUNCH;
+        const size_t sh = (size_t)((kC0StatFrames - 1) * s0 + k0 + kC0MaxK) * sizeof(float);
+        dim3 g((max_frames + kC0StatFrames - 1) / kC0StatFrames, n_utt);
+        if (k10) conv0_gn_stats_kernel<10><<<g, 256, sh, S(stream)>>>(a);
+        else conv0_gn_stats_kernel<kC0MaxK><<<g, 256, sh, S(stream)>>>(a);
         int rc = launch_rc();
         if (rc) return rc;
     }
-    const size_t sh = (size_t)(C * k0 + (kC0Frames - 1) * s0 + k0) * sizeof(float);
-    dim3 g((max_frames + kC0Frames - 1) / kC0Frames, n_utt);
-    conv0_apply_kernel<<<g, 256, sh, S(stream)>>>(a);
+    const size_t sh = (size_t)((kC0ApplyFrames - 1) * s0 + k0 + kC0MaxK) * sizeof(float);
+    dim3 g((max_frames + kC0ApplyFrames - 1) / kC0ApplyFrames, n_utt);
+    if (k10) conv0_apply_kernel<10><<<g, 256, sh, S(stream)>>>(a);
+    else conv0_apply_kernel<kC0MaxK><<<g, 256, sh, S(stream)>>>(a);
     return launch_rc();
 }
 
@@ -393,6 +508,24 @@ extern "C" int w2v_layer_norm(const void* in, int in_f16, long long ld_in, long 
     const int warps = 8;
     const unsigned grid = (unsigned)((total + warps - 1) / warps);
     const int nb = rows ? n_batch : 1;
+    const uintptr_t align = reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(w) |
+                            reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(out32) |
+                            reinterpret_cast<uintptr_t>(out16);
+    const bool vec_ok = D % 128 == 0 && (align % 16) == 0 && ld_in % 4 == 0 && ld_out % 4 == 0;
+#define W2V_LN_VEC(NV)                                                                                          \
+    case NV:                                                                                                    \
+        layer_norm_vec_kernel<NV><<<grid, warps * 32, 0, S(stream)>>>(in, in_f16, ld_in, in_batch_rows, rows,    \
+                                                                      out_off, nb, n_rows, w, b, gelu, out32,   \
+                                                                      (__half*)out16, ld_out);                  \
+        return launch_rc();
+    if (vec_ok) {
+        switch (D / 128) {
+            W2V_LN_VEC(1) W2V_LN_VEC(2) W2V_LN_VEC(3) W2V_LN_VEC(4) W2V_LN_VEC(5) W2V_LN_VEC(6) W2V_LN_VEC(8)
+            W2V_LN_VEC(10) W2V_LN_VEC(12) W2V_LN_VEC(16)
+            default: break;
+        }
+    }
+#undef W2V_LN_VEC
     if (D <= 16 * 32)
         layer_norm_kernel<16><<<grid, warps * 32, 0, S(stream)>>>(in, in_f16, ld_in, in_batch_rows, rows, out_off,
                                                                   nb, n_rows, D, w, b, gelu, out32,

@@ -15,10 +15,11 @@
 //   D  fp32 accumulators in TMEM, two buffers so the epilogue of tile i
 //      overlaps the MMAs of tile i+1.
 //
-// Roles (192 threads, one CTA per SM, persistent over output tiles):
+// Roles (320 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: STAGES-deep smem ring, mbarrier full/empty.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
-//   warps 2..5  epilogue: tcgen05.ld -> bias / GELU / residual -> global.
+//   warps 2..9  epilogue: tcgen05.ld -> bias / GELU / residual -> global;
+//               two warps per TMEM lane quarter, each taking half the columns.
 // Every mbarrier wait is bounded (common.cuh); on expiry the kernel records
 // an error code and returns.
 #include "common.cuh"
@@ -29,6 +30,8 @@ namespace w2v {
 constexpr int kBM = 128;       // tile rows (UMMA M)
 constexpr int kBK = 64;        // K per stage (128 B of fp16: one swizzle row)
 constexpr int kUmmaK = 16;     // K per tcgen05.mma kind::f16
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 struct GemmParams {
     int vec;              // 16-byte vector stores/loads are aligned for this C / resid
@@ -70,7 +73,9 @@ W2V_DEV void epilogue_chunk(const GemmParams& p, long long out_row, long long re
                 v[4 * j] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
             }
         } else {
-            for (int j = 0; j < 32 && col0 + j < p.N; j++) v[j] += __ldg(p.bias + col0 + j);
+            
+#pragma unroll
+            for (int j = 0; j < 32; j++) if (col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
         }
     }
     if (EPI == W2V_EPI_F16_GELU) {
@@ -86,7 +91,9 @@ W2V_DEV void epilogue_chunk(const GemmParams& p, long long out_row, long long re
                 v[4 * j] += x.x; v[4 * j + 1] += x.y; v[4 * j + 2] += x.z; v[4 * j + 3] += x.w;
             }
         } else {
-            for (int j = 0; j < 32 && col0 + j < p.N; j++) v[j] += r[j];
+            
+#pragma unroll
+            for (int j = 0; j < 32; j++) if (col0 + j < p.N) v[j] += r[j];
         }
     }
     if (EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU) {
@@ -102,7 +109,9 @@ W2V_DEV void epilogue_chunk(const GemmParams& p, long long out_row, long long re
                 reinterpret_cast<uint4*>(c)[j] = u;
             }
         } else {
-            for (int j = 0; j < 32 && col0 + j < p.N; j++) c[j] = __float2half_rn(v[j]);
+            
+#pragma unroll
+            for (int j = 0; j < 32; j++) if (col0 + j < p.N) c[j] = __float2half_rn(v[j]);
         }
     } else {
         float* c = reinterpret_cast<float*>(p.C) + out_row * p.ldc + col0;
@@ -111,13 +120,15 @@ W2V_DEV void epilogue_chunk(const GemmParams& p, long long out_row, long long re
             for (int j = 0; j < 8; j++)
                 reinterpret_cast<float4*>(c)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         } else {
-            for (int j = 0; j < 32 && col0 + j < p.N; j++) c[j] = v[j];
+            
+#pragma unroll
+            for (int j = 0; j < 32; j++) if (col0 + j < p.N) c[j] = v[j];
         }
     }
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
     using Cfg = GemmCfg<BN>;
     constexpr int S = Cfg::kStages;
@@ -138,7 +149,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 4); }
+        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], kEpiWarps); }
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
@@ -206,6 +217,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         __syncwarp();
     } else {
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int half = (warp - 2) >> 2;       // which half of the tile's columns
+        constexpr int kChunks = BN / 32 / 2;    // 32-column chunks per warp
         const int r_in_tile = q * 32 + lane;
         int it = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, it++) {
@@ -220,7 +233,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const bool valid = row < p.m_valid;
             const long long out_row = (long long)b * p.c_batch_rows + row;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; c++) {
+            for (int c = half * kChunks; c < (half + 1) * kChunks; c++) {
                 float v[32];
                 tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN + c * 32), v);
                 const int col0 = ni * BN + c * 32;
@@ -238,6 +251,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tc_fence_after();
         tmem_dealloc(tmem_base, Cfg::kTmemCols);
     }
+}
+
+// Self-test of the bounded wait: one thread waits on an mbarrier that nothing
+// ever arrives on; the wait expires after limit_ns, records the error code and
+// the kernel returns normally (no trap), leaving the context usable.
+__global__ void wait_selftest_kernel(int* err, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait_for(&bar, 0, err, limit_ns);
 }
 
 // ── host side ───────────────────────────────────────────────────────────────
@@ -291,7 +317,7 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPar
     }
     const int total = p.n_batch * p.m_tiles * p.n_tiles;
     const int grid = total < sm_count() ? total : sm_count();
-    kern<<<grid, 192, Cfg::kSmem, st>>>(ta, tb, p);
+    kern<<<grid, kThreads, Cfg::kSmem, st>>>(ta, tb, p);
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
@@ -325,6 +351,13 @@ static int pick_bn(int N, long long m_tiles_total) {
 }  // namespace w2v
 
 using namespace w2v;
+
+extern "C" int w2v_selftest_wait_timeout(int* err, int limit_ms, void* stream) {
+    if (!err || limit_ms <= 0 || limit_ms > 2000) return W2V_ERR_ARGS;
+    wait_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        err, (unsigned long long)limit_ms * 1000000ull);
+    return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
+}
 
 extern "C" int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_stride, long long a_row_stride,
                             long long a_rows_in, long long a_batches, long long a_batch_stride, const void* B,
