@@ -184,6 +184,26 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ── sharding helpers (one process per GPU, weak scaling) ─────────────────────
+
+def rank_seeds(rank: int, n_rot: int, batch: int) -> list[list[int]]:
+    """Utterance seeds of this rank's n_rot batches: disjoint across ranks, so
+    N ranks process N different sets of utterances (no shared state)."""
+    base = rank * n_rot * batch
+    return [[base + j * batch + i for i in range(batch)] for j in range(n_rot)]
+
+
+def max_over_ranks(values, world: int, device=None):
+    """Element-wise max of per-rank timings (the whole job is as slow as its
+    slowest rank); identity when world == 1."""
+    import torch
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
 # ── our engine ────────────────────────────────────────────────────────────────
 
 def run_ours(args):
@@ -212,9 +232,7 @@ def run_ours(args):
 
     n = int(args.seconds * SR)
     n_rot = 4
-    base_seed = rank * n_rot * args.batch
-    host_batches = [[s.make_audio(n, base_seed + j * args.batch + i) for i in range(args.batch)]
-                    for j in range(n_rot)]
+    host_batches = [[s.make_audio(n, sd) for sd in seeds] for seeds in rank_seeds(rank, n_rot, args.batch)]
     dev_batches = [torch.from_numpy(np.concatenate(hb)).cuda() for hb in host_batches]
     lens = [n] * args.batch
     stream = torch.cuda.Stream()
@@ -262,14 +280,12 @@ def run_ours(args):
         e2e_s = time.perf_counter() - t0
         barrier()
 
-    stats = torch.tensor([elapsed_ms, e2e_s or 0.0], dtype=torch.float64, device="cuda")
+    elapsed_ms, e2e_s = max_over_ranks([elapsed_ms, e2e_s or 0.0], world, device="cuda")
     if world > 1:
-        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         all_clocks = [None] * world
         dist.all_gather_object(all_clocks, clocks)
     else:
         all_clocks = [clocks]
-    elapsed_ms, e2e_s = float(stats[0]), float(stats[1])
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -351,7 +367,7 @@ def run_kernel_case(args):
         out = torch.empty(B * T, H, device="cuda", dtype=torch.float16)
         off = torch.arange(B, device="cuda", dtype=torch.int64) * T
         Tt = torch.full((B,), T, device="cuda", dtype=torch.int32)
-        fn = lambda: K.attention(qkv.data_ptr(), out.data_ptr(), off.data_ptr(), Tt.data_ptr(), B, H, nh, T, st)
+        fn = lambda: K.attention(qkv.data_ptr(), out.data_ptr(), off.data_ptr(), Tt.data_ptr(), B, H, nh, T, B * T, 0, st)
         flops = 4.0 * B * T * T * H
     else:
         H, G, Kp, T, B = 768, 16, 128, 499, 64

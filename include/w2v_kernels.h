@@ -124,9 +124,11 @@ int w2v_pos_conv(float* x, const float* xin, const long long* off, const int* T,
 /* Bidirectional multi-head attention (src/wav2vec2.cpp:293-334), flash-style
  * online softmax in fp32, fp16 tensor-core products.  qkv: fp16 [M, 3H]
  * (q | k | v, head h at columns h*d..), out: fp16 [M, H].  Keys are limited
- * to the query's own utterance (rows off[u] .. off[u]+T[u]). */
+ * to the query's own utterance (rows off[u] .. off[u]+T[u]).  M = total rows
+ * of qkv.  Head dims 64 and 128 run on tcgen05 (TMEM accumulators, bounded
+ * waits reporting through err); head dim 80 on warp-level mma.sync. */
 int w2v_attention(const void* qkv, void* out, const long long* off, const int* T, int n_utt, int H,
-                  int n_heads, int max_T, void* stream);
+                  int n_heads, int max_T, long long M, int* err, void* stream);
 
 /* Greedy CTC (src/ops.h:132-149): per frame argmax (first max wins), run
  * collapse into spans (id, t_start, t_end), blank runs kept.  logits fp32

@@ -219,7 +219,7 @@ def test_pos_conv(K, H, G, Kp):
         assert np.abs(got[off[u]:off[u] + t] - ref).max() < 2e-4 * (1 + np.abs(ref).max())
 
 
-@pytest.mark.parametrize("H,nh", [(768, 12), (1280, 16), (128, 2)])
+@pytest.mark.parametrize("H,nh", [(768, 12), (1280, 16), (128, 2), (1024, 8), (64, 1)])
 def test_attention(K, H, nh):
     """Flash attention vs fp64 softmax(QK^T/sqrt(d))V per utterance
     (src/wav2vec2.cpp:304-334)."""
@@ -230,9 +230,11 @@ def test_attention(K, H, nh):
     qkv = (rng.standard_normal((M, 3 * H)) * 1.5).astype(np.float16)
     out = torch.zeros(M, H, device="cuda", dtype=torch.float16)
     d_qkv, d_off, d_T = dev(qkv), dev(off), dev(np.array(T, np.int32))
-    K.attention(d_qkv.data_ptr(), out.data_ptr(), d_off.data_ptr(), d_T.data_ptr(), len(T), H, nh, max(T),
-                stream())
+    err = err_word()
+    K.attention(d_qkv.data_ptr(), out.data_ptr(), d_off.data_ptr(), d_T.data_ptr(), len(T), H, nh, max(T), M,
+                err.data_ptr(), stream())
     torch.cuda.synchronize()
+    assert int(err.item()) == 0
     got = out.float().cpu().numpy()
     d = H // nh
     q = torch.from_numpy(qkv[:, :H].astype(np.float64))

@@ -66,7 +66,7 @@ SIGNATURES = {
                                _vp]),
     "w2v_layer_norm": (_i, [_vp, _i, _ll, _ll, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _ll, _vp]),
     "w2v_pos_conv": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp]),
-    "w2v_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "w2v_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _ll, _vp, _vp]),
     "w2v_ctc_greedy": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
 }
 
@@ -265,9 +265,9 @@ class kernels:
                       "w2v_pos_conv")
 
     @staticmethod
-    def attention(qkv, out, off, T, n_utt, H, n_heads, max_T, stream=0):
-        kernels.check(lib().w2v_attention(qkv, out, off, T, n_utt, H, n_heads, max_T, stream or None),
-                      "w2v_attention")
+    def attention(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err=0, stream=0):
+        kernels.check(lib().w2v_attention(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err or None,
+                                          stream or None), "w2v_attention")
 
     @staticmethod
     def ctc_greedy(logits, off, T, n_utt, V, ids, spans, n_spans, max_T, stream=0):

@@ -4,6 +4,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <stdexcept>
+#include <thread>
 
 #include "w2v_kernels.h"
 
@@ -531,7 +532,7 @@ void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, 
     };
     auto attention = [&] {
         launch(P_ATTN, attn_flops, st, "attention",
-               [&] { return w2v_attention(qkv_.p, attn_.p, d_T_off_, d_T_, B, H, n_heads, g.T_max, st); });
+               [&] { return w2v_attention(qkv_.p, attn_.p, d_T_off_, d_T_, B, H, n_heads, g.T_max, M, err, st); });
     };
     if (!c.stable) {
         // post-LN encoder (src/wav2vec2.cpp:360-373)
@@ -588,11 +589,33 @@ void Engine::run_host(const std::vector<const float*>& audio, const std::vector<
         cuda_check(cudaMallocHost(&h_audio_, std::max<size_t>(total, 1) * sizeof(float)), "cudaMallocHost");
         h_audio_n_ = total;
     }
-    for (int u = 0; u < g.n_utt; u++)
-        if (n_samples[u]) memcpy(h_audio_ + g.audio_off[u], audio[u], (size_t)n_samples[u] * sizeof(float));
     audio_stage_.ensure(std::max<size_t>(total, 1) * sizeof(float));
-    cuda_check(cudaMemcpyAsync(audio_stage_.p, h_audio_, total * sizeof(float), cudaMemcpyHostToDevice, stream_),
-               "audio upload");
+    // Pack the caller's (pageable) utterances into pinned staging on several
+    // host threads; each thread uploads its contiguous range as soon as it is
+    // packed, so the host copies overlap the DMA of earlier ranges.
+    const int hw = (int)std::max(1u, std::thread::hardware_concurrency());
+    const int nt = std::max(1, std::min({8, hw / 2, g.n_utt}));
+    std::vector<std::thread> packers;
+    std::vector<int> rc(nt, 0);
+    auto pack = [&](int t) {
+        const int u0 = (int)((long long)g.n_utt * t / nt), u1 = (int)((long long)g.n_utt * (t + 1) / nt);
+        if (u0 >= u1) return;
+        if (cudaSetDevice(device_) != cudaSuccess) { rc[t] = 1; return; }   // the runtime's device is per thread
+        for (int u = u0; u < u1; u++)
+            if (n_samples[u]) memcpy(h_audio_ + g.audio_off[u], audio[u], (size_t)n_samples[u] * sizeof(float));
+        const long long b0 = g.audio_off[u0], b1 = g.audio_off[u1 - 1] + n_samples[u1 - 1];
+        if (b1 > b0)
+            rc[t] = cudaMemcpyAsync(audio_stage_.as<float>() + b0, h_audio_ + b0, (size_t)(b1 - b0) * sizeof(float),
+                                    cudaMemcpyHostToDevice, stream_) != cudaSuccess;
+    };
+    if (nt == 1) {
+        pack(0);
+    } else {
+        for (int t = 0; t < nt; t++) packers.emplace_back(pack, t);
+        for (auto& th : packers) th.join();
+    }
+    for (int r : rc)
+        if (r) throw std::runtime_error("audio upload failed");
     forward(audio_stage_.as<float>(), g, stream_);
     if (g.M > 0) {
         if (logits) {

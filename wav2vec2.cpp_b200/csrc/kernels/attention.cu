@@ -7,8 +7,10 @@
 // unpadded single-utterance computation.
 //
 // fp16 Q/K/V/P operands with fp32 accumulation and fp32 softmax statistics.
-// Tile: 64 queries x 64 keys per step, 4 warps x 16 query rows, K/V double
-// buffered with cp.async.
+// Two implementations: head dims 64 and 128 run the tcgen05 kernel below
+// (attn_tc_kernel); head dim 80 (XLS-R-1B) runs the warp-level mma.sync
+// kernel (attn_kernel: 64 queries x 64 keys per step, 4 warps x 16 query
+// rows, K/V double buffered with cp.async).
 #include "common.cuh"
 #include "w2v_kernels.h"
 
@@ -174,6 +176,282 @@ attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, const long
     }
 }
 
+// ── tcgen05 flash attention (head dim 64 or 128) ────────────────────────────
+// One CTA per (utterance, head, 128-query tile); 192 threads:
+//   warp 0      TMA: Q once, then K/V tiles of 128 keys through a 2-stage ring
+//   warp 1      one thread issues tcgen05.mma: S = Q K^T into TMEM, then
+//               O += P V with P (fp16, smem, K-major) and V straight from its
+//               TMA tile as an MN-major operand
+//   warps 2..5  softmax, one query row per thread (its TMEM lane): online
+//               max/sum in fp32, P written to smem in the 128-byte swizzle
+//               layout, O rescaled in TMEM when the running max moves.
+// Handoffs use mbarriers with bounded waits.  TMEM: S at columns 0..127, O at
+// 128..128+D.
+template <int D>
+struct AttnTc {
+    static constexpr int kAtoms = D / 64;               // 64-column swizzle atoms per row
+    static constexpr int kTile = 128 * D * 2;           // one Q, K or V tile
+    static constexpr int kAtomBytes = 128 * 64 * 2;     // 16 KB
+    static constexpr int kPBytes = 128 * 128 * 2;       // P: 2 atoms of 64 keys
+    // D = 64: one K/V stage keeps the CTA at ~81 KB so two CTAs share an SM and
+    // hide each other's loads; D = 128: two stages, one CTA per SM.
+    static constexpr int kStages = D == 64 ? 1 : 2;
+    static constexpr int kSmem = kTile + kStages * 2 * kTile + kPBytes + 1024 + 128;
+    static constexpr int kTmemCols = 256;
+};
+
+template <int D>
+__global__ void __launch_bounds__(192)
+attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out, const long long* __restrict__ off,
+               const int* __restrict__ Tn, int H, float scale_log2, int* err) {
+    using Cfg = AttnTc<D>;
+    const int u = blockIdx.z, h = blockIdx.y;
+    const int T = Tn[u];
+    const int q0 = blockIdx.x * 128;
+    if (q0 >= T) return;
+    const long long base = off[u];
+    const int n_kv = (T + 127) / 128;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    uint8_t* sQ = smem;
+    uint8_t* sKV = sQ + Cfg::kTile;
+    uint8_t* sP = sKV + Cfg::kStages * 2 * Cfg::kTile;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + Cfg::kPBytes);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;                     // [kStages]
+    uint64_t* kv_empty = bars + 1 + Cfg::kStages;     // [kStages]
+    uint64_t* s_full = bars + 1 + 2 * Cfg::kStages;
+    uint64_t* s_free = s_full + 1;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* o_done = s_full + 3;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < Cfg::kStages; s++) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 4);
+        mbar_init(p_full, 4);
+        mbar_init(o_done, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tm);
+    }
+    if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t tS = tmem_base, tO = tmem_base + 128;
+    const int colQ = h * D, colK = H + h * D, colV = 2 * H + h * D;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            mbar_arrive_expect_tx(q_full, Cfg::kTile);
+#pragma unroll
+            for (int a = 0; a < Cfg::kAtoms; a++)
+                tma_load_2d(sQ + a * Cfg::kAtomBytes, &tm, q_full, colQ + 64 * a, (int)(base + q0));
+            int stage = 0;
+            uint32_t phase = 0, issued = 0, last_par = 0;
+            for (int j = 0; j < n_kv; j++) {
+                if (!mbar_wait(&kv_empty[stage], phase ^ 1u, err)) break;
+                mbar_arrive_expect_tx(&kv_full[stage], 2 * Cfg::kTile);
+                uint8_t* sK = sKV + stage * 2 * Cfg::kTile;
+                uint8_t* sV = sK + Cfg::kTile;
+#pragma unroll
+                for (int a = 0; a < Cfg::kAtoms; a++) {
+                    tma_load_2d(sK + a * Cfg::kAtomBytes, &tm, &kv_full[stage], colK + 64 * a, (int)(base + j * 128));
+                    tma_load_2d(sV + a * Cfg::kAtomBytes, &tm, &kv_full[stage], colV + 64 * a, (int)(base + j * 128));
+                }
+                issued |= 1u << stage;
+                last_par = (last_par & ~(1u << stage)) | (phase << stage);
+                if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+            }
+            mbar_wait(q_full, 0, err);
+            for (int s = 0; s < Cfg::kStages; s++)
+                if (issued & (1u << s)) mbar_wait(&kv_full[s], (last_par >> s) & 1u, err);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            constexpr uint32_t idesc_s = umma_idesc_f16(128, 128);
+            constexpr uint32_t idesc_o = umma_idesc_f16_bmn(128, D);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = mbar_wait(q_full, 0, err);
+            for (int j = 0; j < n_kv && ok; j++) {
+                if (!mbar_wait(&kv_full[stage], phase, err)) break;
+                if (j > 0 && !mbar_wait(s_free, (uint32_t)(j - 1) & 1u, err)) break;
+                tc_fence_after();
+                const uint32_t q_addr = smem_u32(sQ);
+                const uint32_t k_addr = smem_u32(sKV + stage * 2 * Cfg::kTile);
+                const uint32_t v_addr = k_addr + Cfg::kTile;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; kk++) {
+                    const uint32_t o = (kk / 4) * Cfg::kAtomBytes + (kk % 4) * 32;
+                    umma_f16(tS, umma_desc_sw128(q_addr + o), umma_desc_sw128(k_addr + o), idesc_s, kk > 0);
+                }
+                umma_commit(s_full);
+                if (!mbar_wait(p_full, (uint32_t)j & 1u, err)) break;
+                tc_fence_after();
+                const uint32_t p_addr = smem_u32(sP);
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t po = (kk / 4) * Cfg::kAtomBytes + (kk % 4) * 32;
+                    umma_f16(tO, umma_desc_sw128(p_addr + po), umma_desc_sw128_mn(v_addr + kk * 2048, Cfg::kAtomBytes),
+                             idesc_o, (j > 0 || kk > 0));
+                }
+                umma_commit(&kv_empty[stage]);
+                umma_commit(o_done);
+                if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+            }
+        }
+        __syncwarp();
+    } else {
+        const int qd = warp & 3;                       // TMEM lane quarter
+        const int row = qd * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_kv && ok; j++) {
+            if (!mbar_wait(s_full, (uint32_t)j & 1u, err)) { ok = false; break; }
+            tc_fence_after();
+            float sv[128];
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float t[32];
+                tmem_ld32(tS + lane_off + c * 32, t);
+#pragma unroll
+                for (int i = 0; i < 32; i++) sv[c * 32 + i] = t[i];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
+            const int kb = j * 128;
+            if (kb + 128 > T) {
+#pragma unroll
+                for (int c = 0; c < 128; c++)
+                    if (kb + c >= T) sv[c] = -INFINITY;
+            }
+            float mx = m;
+#pragma unroll
+            for (int c = 0; c < 128; c++) mx = fmaxf(mx, sv[c]);
+            const float alpha = exp2f((m - mx) * scale_log2);
+            const float mxs = mx * scale_log2;
+            float sum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 128; c++) {
+                sv[c] = exp2f(fmaf(sv[c], scale_log2, -mxs));
+                sum += sv[c];
+            }
+            l = l * alpha + sum;
+            m = mx;
+            if (j > 0) {
+                if (!mbar_wait(o_done, (uint32_t)(j - 1) & 1u, err)) { ok = false; break; }
+                tc_fence_after();
+            }
+            // P row -> smem (fp16, K-major, 128-byte swizzle: chunk c8 of row r at (c8 ^ (r & 7)))
+#pragma unroll
+            for (int ch = 0; ch < 16; ch++) {
+                uint4 pk;
+                pk.x = pack_half2(sv[ch * 8 + 0], sv[ch * 8 + 1]);
+                pk.y = pack_half2(sv[ch * 8 + 2], sv[ch * 8 + 3]);
+                pk.z = pack_half2(sv[ch * 8 + 4], sv[ch * 8 + 5]);
+                pk.w = pack_half2(sv[ch * 8 + 6], sv[ch * 8 + 7]);
+                uint8_t* dst = sP + (ch / 8) * Cfg::kAtomBytes + row * 128 + (((ch % 8) ^ (row & 7)) * 16);
+                *reinterpret_cast<uint4*>(dst) = pk;
+            }
+            // rescale the running output when any row's max moved
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                for (int a = 0; a < D / 32; a++) {
+                    float t[32];
+                    tmem_ld32(tO + lane_off + a * 32, t);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) t[i] *= alpha;
+                    tmem_st32(tO + lane_off + a * 32, t);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+        }
+        if (ok && mbar_wait(o_done, (uint32_t)(n_kv - 1) & 1u, err)) {
+            tc_fence_after();
+            const float inv = 1.f / l;
+            const bool valid = q0 + row < T;
+            __half* o = out + (base + q0 + row) * (long long)H + (long long)h * D;
+#pragma unroll
+            for (int a = 0; a < D / 32; a++) {
+                float t[32];
+                tmem_ld32(tO + lane_off + a * 32, t);
+                if (valid) {
+#pragma unroll
+                    for (int v = 0; v < 4; v++) {
+                        uint4 pk;
+                        pk.x = pack_half2(t[8 * v + 0] * inv, t[8 * v + 1] * inv);
+                        pk.y = pack_half2(t[8 * v + 2] * inv, t[8 * v + 3] * inv);
+                        pk.z = pack_half2(t[8 * v + 4] * inv, t[8 * v + 5] * inv);
+                        pk.w = pack_half2(t[8 * v + 6] * inv, t[8 * v + 7] * inv);
+                        *reinterpret_cast<uint4*>(o + a * 32 + v * 8) = pk;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
+
+template <int D>
+static int launch_attn_tc(const void* qkv, void* out, const long long* off, const int* T, int n_utt, int H,
+                          int n_heads, int max_T, long long M, int* err, cudaStream_t st) {
+    using Cfg = AttnTc<D>;
+    auto enc = attn_encode_fn();
+    if (!enc) return W2V_ERR_DRIVER;
+    CUtensorMap tm;
+    const uint64_t dims[2] = {(uint64_t)3 * H, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)3 * H * 2};
+    const uint32_t box[2] = {64, 128};
+    const uint32_t es[2] = {1, 1};
+    if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(qkv), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return W2V_ERR_TENSOR_MAP;
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        if (cudaFuncSetAttribute(attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
+            cudaSuccess)
+            return W2V_ERR_LAUNCH;
+        attr[dev & 63] = true;
+    }
+    const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    dim3 grid((max_T + 127) / 128, n_heads, n_utt);
+    attn_tc_kernel<D><<<grid, 192, Cfg::kSmem, st>>>(tm, (__half*)out, off, T, H, scale_log2, err);
+    return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
+}
+
 template <int D>
 static int launch_attn(const void* qkv, void* out, const long long* off, const int* T, int n_utt, int H,
                        int n_heads, int max_T, cudaStream_t st) {
@@ -196,15 +474,20 @@ static int launch_attn(const void* qkv, void* out, const long long* off, const i
 }  // namespace w2v
 
 extern "C" int w2v_attention(const void* qkv, void* out, const long long* off, const int* T, int n_utt, int H,
-                             int n_heads, int max_T, void* stream) {
-    if (n_heads <= 0 || H % n_heads) return W2V_ERR_ARGS;
-    if (n_utt <= 0 || max_T <= 0) return W2V_OK;
+                             int n_heads, int max_T, long long M, int* err, void* stream) {
+    if (n_heads <= 0 || H % n_heads || M < 0) return W2V_ERR_ARGS;
+    if (n_utt <= 0 || max_T <= 0 || M == 0) return W2V_OK;
     const int d = H / n_heads;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const bool tma_ok = (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && H % 64 == 0;
     switch (d) {
-        case 64: return w2v::launch_attn<64>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
+        case 64:
+            if (tma_ok) return w2v::launch_attn_tc<64>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+            return w2v::launch_attn<64>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         case 80: return w2v::launch_attn<80>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
-        case 128: return w2v::launch_attn<128>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
+        case 128:
+            if (tma_ok) return w2v::launch_attn_tc<128>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+            return w2v::launch_attn<128>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         default: return W2V_ERR_ARGS;
     }
 }

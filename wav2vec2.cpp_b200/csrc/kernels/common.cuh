@@ -170,6 +170,21 @@ W2V_DEV uint64_t umma_desc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     return d;
 }
 
+// 32 lanes x 32 consecutive fp32 columns of TMEM -> 32 registers, without
+// waiting: call tmem_wait_ld() before using any of them.
+W2V_DEV void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+W2V_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // 32 lanes x 32 consecutive fp32 columns of TMEM -> 32 registers per thread.
 W2V_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
@@ -202,6 +217,28 @@ W2V_DEV bool elect_one() {
 // one exp2 and one reciprocal on the special-function unit, relative error
 // ~1e-6 (well below the fp16 rounding of every output it feeds).  Limits:
 // x -> -inf gives -0 (exp overflows to inf), x -> +inf gives x.
+//
+// 2^z on the FMA pipe, for kernels whose special-function unit is saturated:
+// Cody-Waite range reduction z = n + f, |f| <= 1/2, with n obtained by the
+// round-to-nearest trick (adding 1.5 * 2^23), then the degree-6 Taylor
+// polynomial of 2^f = e^(f ln 2) (truncation error <= (ln2 / 2)^7 / 7! ~ 1.2e-7
+// relative) and 2^n applied by adding n to the exponent field.  z is clamped
+// to [-126, 126] so the result stays a normal float.
+W2V_DEV float exp2_fma(float z) {
+    z = fminf(fmaxf(z, -126.0f), 126.0f);
+    const float t = z + 12582912.0f;                       // 1.5 * 2^23: rounds z to an integer
+    const int n = __float_as_int(t) - 0x4B400000;          // that integer, from the mantissa bits
+    const float f = z - (t - 12582912.0f);
+    float p = 1.5403530393381606e-4f;                      // (ln 2)^6 / 720
+    p = fmaf(p, f, 1.3333558146428443e-3f);                // (ln 2)^5 / 120
+    p = fmaf(p, f, 9.6181291076284772e-3f);                // (ln 2)^4 / 24
+    p = fmaf(p, f, 5.5504108664821580e-2f);                // (ln 2)^3 / 6
+    p = fmaf(p, f, 0.24022650695910071f);                  // (ln 2)^2 / 2
+    p = fmaf(p, f, 0.69314718055994531f);                  // ln 2
+    p = fmaf(p, f, 1.0f);
+    return __int_as_float(__float_as_int(p) + (n << 23));
+}
+
 W2V_DEV float gelu_tanh(float x) {
     const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
     return __fdividef(x, 1.0f + __expf(-2.0f * u));
@@ -241,4 +278,113 @@ W2V_DEV void cp_async16(uint32_t saddr, const void* g) {
 W2V_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 W2V_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+}  // namespace w2v
+
+namespace w2v {
+// ── more tcgen05 helpers (attention) ────────────────────────────────────────
+// 32 lanes x 32 consecutive 32-bit TMEM columns <- 32 registers per thread.
+W2V_DEV void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Instruction descriptor for kind::f16 with A K-major and B MN-major
+// (B element (n, k) at n contiguous: e.g. V stored [key][d]).
+__host__ __device__ constexpr uint32_t umma_idesc_f16_bmn(int M, int N) {
+    return umma_idesc_f16(M, N) | (1u << 16);
+}
+
+// MN-major, 128-byte swizzle: rows along K of 128 B (64 fp16 along MN), 8-row
+// atoms of 1024 B (SBO); lbo = byte distance between 64-wide MN atoms.
+W2V_DEV uint64_t umma_desc_sw128_mn(uint32_t saddr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+W2V_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+}  // namespace w2v
+
+namespace w2v {
+// ── CTA-pair (cluster of 2) helpers for cta_group::2 ────────────────────────
+W2V_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+W2V_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same smem location in CTA `rank` of the cluster
+W2V_DEV uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+W2V_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+W2V_DEV void mbar_arrive_expect_tx_addr(uint32_t saddr, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr), "r"(bytes) : "memory");
+}
+// TMA load whose completion is signalled on an mbarrier that may live in the
+// peer CTA of the pair (cluster address).
+W2V_DEV void tma_load_4d_pair(void* smem_dst, const CUtensorMap* m, uint32_t bar_cluster, int c0, int c1, int c2,
+                              int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+W2V_DEV void tma_load_2d_pair(void* smem_dst, const CUtensorMap* m, uint32_t bar_cluster, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(c0), "r"(c1)
+        : "memory");
+}
+W2V_DEV void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+W2V_DEV void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+W2V_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D (256 rows over the CTA pair) (+)= A . B^T, issued by the pair's leader.
+W2V_DEV void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive on an mbarrier (shared::cluster address: this CTA's or the peer's)
+// once every tcgen05 operation this thread issued before has completed.
+W2V_DEV void umma_commit_pair(uint32_t bar_cluster) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+                 : "memory");
+}
 }  // namespace w2v

@@ -95,6 +95,7 @@ constexpr int kC0Group = 32;        // frames per register group
 constexpr int kC0ApplyFrames = 256; // frames per apply block
 constexpr int kC0StatFrames = 1024; // frames per statistics block
 constexpr int kC0MaxK = 16;
+constexpr int kC0K = 10, kC0S = 5, kC0Sub = 8, kC0Win = (kC0Sub - 1) * kC0S + kC0K;   // 45
 
 struct Conv0Args {
     const float* audio; const long long* off; const int* len; const int* frames;
@@ -107,7 +108,7 @@ W2V_DEV void conv0_stage(const Conv0Args& a, int u, int f0, int nf, float* xs) {
     const float mean = a.stats[2 * u], inv = a.stats[2 * u + 1];
     const float* x = a.audio + a.off[u];
     const int ns = (nf - 1) * a.s0 + a.k0;
-    for (int i = threadIdx.x; i < ns + kC0MaxK; i += blockDim.x)
+    for (int i = threadIdx.x; i < ns + kC0MaxK + kC0Win; i += blockDim.x)
         xs[i] = i < ns ? (x[(long long)f0 * a.s0 + i] - mean) * inv : 0.f;
 }
 
@@ -315,6 +316,165 @@ __global__ void layer_norm_kernel(const void* __restrict__ in, int in_f16, long 
     }
 }
 
+// Specialised conv 0 for the published extractor shape (kernel 10, stride 5):
+// 128 threads, thread t owns channels 4t..4t+3 (40 taps in registers) and
+// computes 8 frames at a time from a 45-sample window held in registers, so a
+// broadcast shared-memory load feeds 32 FMAs instead of 2.  Same arithmetic
+// order per output as conv0_group (bias, then taps 0..K-1).
+
+W2V_DEV void conv0x4_sub(const float* xs, int f, const float (&w)[4][kC0K], const float (&bb)[4],
+                         float (&y)[kC0Sub][4]) {
+    float xr[kC0Win];
+#pragma unroll
+    for (int i = 0; i < kC0Win; i++) xr[i] = xs[f * kC0S + i];
+#pragma unroll
+    for (int fr = 0; fr < kC0Sub; fr++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            float acc = bb[c];
+#pragma unroll
+            for (int k = 0; k < kC0K; k++) acc = fmaf(xr[fr * kC0S + k], w[c][k], acc);
+            y[fr][c] = acc;
+        }
+}
+
+W2V_DEV void conv0x4_load(const Conv0Args& a, int c0, float (&w)[4][kC0K], float (&bb)[4]) {
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+#pragma unroll
+        for (int k = 0; k < kC0K; k++) w[c][k] = __ldg(a.w0 + (c0 + c) * kC0K + k);
+        bb[c] = a.b0 ? __ldg(a.b0 + c0 + c) : 0.f;
+    }
+}
+
+__global__ void __launch_bounds__(128) conv0x4_gn_stats_kernel(Conv0Args a) {
+    extern __shared__ float xs[];
+    const int u = blockIdx.y;
+    const int F = a.frames[u];
+    const int f0 = blockIdx.x * kC0StatFrames;
+    if (f0 >= F) return;
+    const int nf = min(kC0StatFrames, F - f0);
+    conv0_stage(a, u, f0, nf, xs);
+    __syncthreads();
+    const int c0 = 4 * threadIdx.x;
+    if (c0 >= a.C) return;
+    float w[4][kC0K], bb[4];
+    conv0x4_load(a, c0, w, bb);
+    double s[4] = {0, 0, 0, 0}, q[4] = {0, 0, 0, 0};
+    for (int g = 0; g < nf; g += 32) {
+        float ps[4] = {0, 0, 0, 0}, pq[4] = {0, 0, 0, 0};     // fp32 within <= 32 frames
+#pragma unroll 1
+        for (int f = g; f < g + 32; f += kC0Sub) {
+            float y[kC0Sub][4];
+            conv0x4_sub(xs, f, w, bb, y);
+#pragma unroll
+            for (int fr = 0; fr < kC0Sub; fr++)
+                if (f + fr < nf)
+#pragma unroll
+                    for (int c = 0; c < 4; c++) { ps[c] += y[fr][c]; pq[c] = fmaf(y[fr][c], y[fr][c], pq[c]); }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; c++) { s[c] += ps[c]; q[c] += pq[c]; }
+    }
+    double* gp = a.gn + ((long long)u * a.C + c0) * 2;
+#pragma unroll
+    for (int c = 0; c < 4; c++) { atomicAdd(gp + 2 * c, s[c]); atomicAdd(gp + 2 * c + 1, q[c]); }
+}
+
+__global__ void __launch_bounds__(128) conv0x4_apply_kernel(Conv0Args a) {
+    extern __shared__ float xs[];
+    __shared__ float red[4][kC0Sub];
+    __shared__ float rowstat[2][kC0Sub];
+    const int u = blockIdx.y;
+    const int F = a.frames[u];
+    const int f0 = blockIdx.x * kC0ApplyFrames;
+    if (f0 >= F) return;
+    const int nf = min(kC0ApplyFrames, F - f0);
+    conv0_stage(a, u, f0, nf, xs);
+    __syncthreads();
+    const int c0 = 4 * threadIdx.x;
+    const bool active = c0 < a.C;
+    float w[4][kC0K], bb[4];
+    float m[4], iv[4], ga[4], be[4];
+#pragma unroll
+    for (int c = 0; c < 4; c++) { m[c] = 0.f; iv[c] = 1.f; ga[c] = 1.f; be[c] = 0.f; bb[c] = 0.f; }
+    if (active) {
+        conv0x4_load(a, c0, w, bb);
+        if (a.norm) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) { ga[c] = a.gw[c0 + c]; be[c] = a.gb[c0 + c]; }
+        }
+        if (a.norm == 1) {
+            const double* gp = a.gn + ((long long)u * a.C + c0) * 2;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const double mu = gp[2 * c] / F;
+                const float var = (float)fmax(gp[2 * c + 1] / F - mu * mu, 0.0);
+                m[c] = (float)mu;
+                iv[c] = 1.f / sqrtf(var + 1e-5f);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+            for (int k = 0; k < kC0K; k++) w[c][k] = 0.f;
+    }
+    const int wi = threadIdx.x >> 5, l = threadIdx.x & 31;
+#pragma unroll 1
+    for (int f = 0; f < nf; f += kC0Sub) {
+        float y[kC0Sub][4];
+        conv0x4_sub(xs, f, w, bb, y);
+        if (a.norm == 2) {
+            // LayerNorm over channels per frame (src/ops.h:24-36), two-pass
+            for (int pass = 0; pass < 2; pass++) {
+#pragma unroll
+                for (int fr = 0; fr < kC0Sub; fr++) {
+                    float v = 0.f;
+                    if (active) {
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            const float d = pass == 0 ? y[fr][c] : y[fr][c] - rowstat[0][fr];
+                            v += pass == 0 ? d : d * d;
+                        }
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (l == 0) red[wi][fr] = v;
+                }
+                __syncthreads();
+                if (threadIdx.x < kC0Sub) {
+                    float sum = 0.f;
+                    for (int i = 0; i < (int)(blockDim.x >> 5); i++) sum += red[i][threadIdx.x];
+                    if (pass == 0) rowstat[0][threadIdx.x] = sum / a.C;
+                    else rowstat[1][threadIdx.x] = 1.f / sqrtf(sum / a.C + 1e-5f);
+                }
+                __syncthreads();
+            }
+        }
+        if (active) {
+#pragma unroll
+            for (int fr = 0; fr < kC0Sub; fr++) {
+                if (f + fr < nf) {
+                    float v[4];
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        v[c] = y[fr][c];
+                        if (a.norm == 1) v[c] = (v[c] - m[c]) * iv[c] * ga[c] + be[c];
+                        else if (a.norm == 2) v[c] = (v[c] - rowstat[0][fr]) * rowstat[1][fr] * ga[c] + be[c];
+                        v[c] = gelu_tanh(v[c]);
+                    }
+                    uint2 pk;
+                    pk.x = pack_half2(v[0], v[1]);
+                    pk.y = pack_half2(v[2], v[3]);
+                    *reinterpret_cast<uint2*>(a.out + ((long long)u * a.rows_max + f0 + f + fr) * a.C + c0) = pk;
+                }
+            }
+        }
+        if (a.norm == 2) __syncthreads();
+    }
+}
+
 // Vectorised row LayerNorm: warp per row, each lane holds NV groups of 4
 // consecutive columns (D = 128 * NV); 16-byte fp32 / 8-byte fp16 accesses.
 template <int NV>
@@ -481,17 +641,33 @@ extern "C" int w2v_conv0(const float* audio, const long long* off, const int* le
     if (n_utt <= 0 || max_frames <= 0) return W2V_OK;
     Conv0Args a{audio, off, len, frames, stats, w0, b0, C, k0, s0, norm, gw, gb, gn_sums, (__half*)out, rows_max};
     const bool k10 = k0 == 10;
+    if (k0 == kC0K && s0 == kC0S && C % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0) {
+        // published shape: 4 channels per thread, 8-frame register windows
+        if (norm == 1) {
+            if (cudaMemsetAsync(gn_sums, 0, sizeof(double) * 2 * C * (size_t)n_utt, S(stream)) != cudaSuccess)
+                return W2V_ERR_LAUNCH;
+            const size_t sh = (size_t)((kC0StatFrames - 1) * s0 + k0 + kC0MaxK + kC0Win) * sizeof(float);
+            dim3 g((max_frames + kC0StatFrames - 1) / kC0StatFrames, n_utt);
+            conv0x4_gn_stats_kernel<<<g, 128, sh, S(stream)>>>(a);
+            int rc = launch_rc();
+            if (rc) return rc;
+        }
+        const size_t sh = (size_t)((kC0ApplyFrames - 1) * s0 + k0 + kC0MaxK + kC0Win) * sizeof(float);
+        dim3 g((max_frames + kC0ApplyFrames - 1) / kC0ApplyFrames, n_utt);
+        conv0x4_apply_kernel<<<g, 128, sh, S(stream)>>>(a);
+        return launch_rc();
+    }
     if (norm == 1) {
         if (cudaMemsetAsync(gn_sums, 0, sizeof(double) * 2 * C * (size_t)n_utt, S(stream)) != cudaSuccess)
             return W2V_ERR_LAUNCH;
-        const size_t sh = (size_t)((kC0StatFrames - 1) * s0 + k0 + kC0MaxK) * sizeof(float);
+        const size_t sh = (size_t)((kC0StatFrames - 1) * s0 + k0 + kC0MaxK + kC0Win) * sizeof(float);
         dim3 g((max_frames + kC0StatFrames - 1) / kC0StatFrames, n_utt);
         if (k10) conv0_gn_stats_kernel<10><<<g, 256, sh, S(stream)>>>(a);
         else conv0_gn_stats_kernel<kC0MaxK><<<g, 256, sh, S(stream)>>>(a);
         int rc = launch_rc();
         if (rc) return rc;
     }
-    const size_t sh = (size_t)((kC0ApplyFrames - 1) * s0 + k0 + kC0MaxK) * sizeof(float);
+    const size_t sh = (size_t)((kC0ApplyFrames - 1) * s0 + k0 + kC0MaxK + kC0Win) * sizeof(float);
     dim3 g((max_frames + kC0ApplyFrames - 1) / kC0ApplyFrames, n_utt);
     if (k10) conv0_apply_kernel<10><<<g, 256, sh, S(stream)>>>(a);
     else conv0_apply_kernel<kC0MaxK><<<g, 256, sh, S(stream)>>>(a);
