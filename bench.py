@@ -342,7 +342,8 @@ def run_ours(args):
 
 def run_kernel_case(args):
     """One kernel at a representative size (for ncu captures and micro-timing):
-    gemm: encoder fc1 shape (M rows x K=768 -> N=3072, fp16 out, GELU epilogue);
+    gemm: M rows x K -> N with the given epilogue (default the encoder FFN-up
+          shape, K=768 -> N=3072, fp16 out, GELU epilogue);
     attention: 64 utterances x 499 frames, 12 heads x 64;
     pos_conv: the same batch, hidden 768, kernel 128, 16 groups."""
     import torch
@@ -353,13 +354,15 @@ def run_kernel_case(args):
     st = torch.cuda.current_stream().cuda_stream
     M = args.rows
     if args.kernel == "gemm":
-        Kd, N = 768, 3072
+        N, Kd, epi = (int(v) for v in args.gemm_shape.split(","))
         A = torch.randn(M, Kd, device="cuda").half()
         W = (torch.randn(N, Kd, device="cuda") * 0.05).half()
         bias = torch.randn(N, device="cuda")
-        out = torch.empty(M, N, device="cuda", dtype=torch.float16)
+        f16 = epi in (0, 1)
+        out = torch.zeros(M, N, device="cuda", dtype=torch.float16 if f16 else torch.float32)
+        res = out.data_ptr() if epi == 3 else 0
         fn = lambda: K.gemm(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, out.data_ptr(), N, M, M,
-                            bias.data_ptr(), 0, N, 1, 0, 0, st)
+                            bias.data_ptr(), res, N, epi, args.block_n, 0, st)
         flops = 2.0 * M * N * Kd
     elif args.kernel == "attention":
         H, nh, T, B = 768, 12, 499, 64
@@ -390,7 +393,10 @@ def run_kernel_case(args):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    print(json.dumps({"kernel": args.kernel, "rows": M, "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
+    rec = {"kernel": args.kernel, "rows": M, "ms": ms, "tflops": flops / ms / 1e9}
+    if args.kernel == "gemm":
+        rec.update(shape=args.gemm_shape, block_n=args.block_n)
+    print(json.dumps(rec), flush=True)
 
 
 def main():
@@ -411,6 +417,10 @@ def main():
     ap.add_argument("--kernel", choices=["gemm", "attention", "pos_conv"], default=None,
                     help="time one kernel at a representative size instead of the whole step")
     ap.add_argument("--rows", type=int, default=32768, help="GEMM rows for --kernel gemm")
+    ap.add_argument("--gemm-shape", default="3072,768,1",
+                    help="N,K,epilogue for --kernel gemm (epilogue 0 fp16, 1 fp16+GELU, 2 fp32, 3 fp32+residual)")
+    ap.add_argument("--block-n", type=int, default=0,
+                    help="GEMM tile for --kernel gemm: 0 automatic, 64/128/256 one CTA, -128/-256 CTA pair")
     args = ap.parse_args()
     if args.kernel:
         run_kernel_case(args)

@@ -74,6 +74,85 @@ def test_gemm_plain(K, M, N, Kd, epi, bn):
     assert (d <= tol).all(), f"max err {d.max().item()}"
 
 
+@pytest.mark.parametrize("M,N,Kd,epi,bn", [
+    (1, 256, 64, EPI_F32, -256), (255, 256, 768, EPI_F16, -256), (257, 512, 768, EPI_F32_RESID, -256),
+    (20000, 2304, 768, EPI_F16, -256), (9000, 768, 3072, EPI_F32_RESID, -256), (7777, 3072, 768, EPI_F16_GELU, -256),
+    (9000, 768, 768, EPI_F32_RESID, -128), (300, 200, 512, EPI_F32, -256), (513, 96, 256, EPI_F16, -128),
+    (4000, 1280, 1280, EPI_F16_GELU, -128)])
+def test_gemm_cta_pair(K, M, N, Kd, epi, bn):
+    """CTA-pair (cta_group::2) tiles of 256 x |bn|: ragged M and N, several
+    tiles per pair (both TMEM accumulators in turn), every epilogue."""
+    g = torch.Generator(device="cuda").manual_seed(M * 11 + N)
+    A = torch.randn(M + 5, Kd, device="cuda", generator=g).half()
+    W = (torch.randn(N, Kd, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(N, device="cuda", generator=g)
+    resid = torch.randn(M, N, device="cuda", generator=g)
+    f16 = epi in (EPI_F16, EPI_F16_GELU)
+    out = torch.full((M + 5, N), float("nan"), device="cuda", dtype=torch.float16 if f16 else torch.float32)
+    err = err_word()
+    K.gemm(A.data_ptr(), Kd, 1, 1, Kd, M + 5, 1, (M + 5) * Kd, W.data_ptr(), N, out.data_ptr(), N, M + 5, M,
+           bias.data_ptr(), resid.data_ptr() if epi == EPI_F32_RESID else 0, N, epi, bn, err.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = A[:M].double() @ W.double().T + bias.double()
+    if epi == EPI_F16_GELU:
+        ref = gelu_t(ref)
+    if epi == EPI_F32_RESID:
+        ref = ref + resid.double()
+    d = (out[:M].double() - ref).abs()
+    tol = (2e-3 if f16 else 1e-4) * (1 + ref.abs())
+    assert torch.isfinite(out[:M]).all()
+    assert (d <= tol).all(), f"max err {d.max().item()}"
+    assert torch.isnan(out[M:]).all(), "rows past m_valid were written"
+
+
+@pytest.mark.parametrize("epi", [EPI_F16_GELU, EPI_F32_RESID])
+@pytest.mark.parametrize("bn", [0, 128, -256])
+def test_gemm_ragged_columns(K, epi, bn):
+    """N not a multiple of 4 inside a wider row pitch: the last column group
+    of each row is stored element by element, columns N..ldc-1 untouched."""
+    M, N, Kd, ldc = 700, 94, 256, 104
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.randn(M, Kd, device="cuda", generator=g).half()
+    W = (torch.randn(N, Kd, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(N + 2, device="cuda", generator=g)
+    f16 = epi == EPI_F16_GELU
+    resid = torch.randn(M, ldc, device="cuda", generator=g)
+    out = torch.full((M, ldc), float("nan"), device="cuda", dtype=torch.float16 if f16 else torch.float32)
+    err = err_word()
+    K.gemm(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, out.data_ptr(), ldc, M, M, bias.data_ptr(),
+           resid.data_ptr() if not f16 else 0, ldc, epi, bn, err.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = A.double() @ W.double().T + bias[:N].double()
+    ref = gelu_t(ref) if f16 else ref + resid[:, :N].double()
+    d = (out[:, :N].double() - ref).abs()
+    assert (d <= (2e-3 if f16 else 1e-4) * (1 + ref.abs())).all(), d.max().item()
+    assert torch.isnan(out[:, N:]).all()
+
+
+@pytest.mark.parametrize("B,C,Lin,k,s,bn", [(3, 512, 1001, 3, 2, -256), (2, 512, 8000, 2, 2, -256),
+                                            (4, 128, 600, 3, 2, -128)])
+def test_gemm_cta_pair_conv_view(K, B, C, Lin, k, s, bn):
+    g = torch.Generator(device="cuda").manual_seed(Lin + 1)
+    Lout = (Lin - k) // s + 1
+    R = Lin + (-Lin) % s
+    x = torch.randn(B, R, C, device="cuda", generator=g).half()
+    w = (torch.randn(C, C, k, device="cuda", generator=g) * 0.05).half()
+    wg = w.permute(0, 2, 1).reshape(C, k * C).contiguous()
+    Rout = Lout + 3
+    out = torch.full((B, Rout, C), float("nan"), device="cuda")
+    err = err_word()
+    K.gemm(x.data_ptr(), C, k, s, C, R, B, R * C, wg.data_ptr(), C, out.data_ptr(), C, Rout, Lout, 0, 0, 0,
+           EPI_F32, bn, err.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = torch.nn.functional.conv1d(x[:, :Lin].double().transpose(1, 2), w.double(), stride=s).transpose(1, 2)
+    d = (out[:, :Lout].double() - ref).abs()
+    assert (d <= 2e-5 * (1 + ref.abs())).all(), d.max().item()
+    assert torch.isnan(out[:, Lout:]).all()
+
+
 @pytest.mark.parametrize("B,C,Lin,k,s", [(3, 128, 257, 3, 2), (2, 512, 1000, 3, 2), (4, 128, 130, 2, 2),
                                          (1, 64, 77, 3, 2)])
 def test_gemm_conv_view(K, B, C, Lin, k, s):

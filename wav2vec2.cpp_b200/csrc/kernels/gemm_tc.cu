@@ -32,6 +32,7 @@ constexpr int kBK = 64;        // K per stage (128 B of fp16: one swizzle row)
 constexpr int kUmmaK = 16;     // K per tcgen05.mma kind::f16
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kStageBytes = kEpiWarps * 32 * 32 * 4;   // epilogue staging, 4 KB per warp
 
 struct GemmParams {
     int vec;              // 16-byte vector stores/loads are aligned for this C / resid
@@ -58,7 +59,7 @@ struct GemmCfg {
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-    static constexpr int kSmem = kStages * (kABytes + kBBytes) + 1024 + 256;
+    static constexpr int kSmem = kStages * (kABytes + kBBytes) + kStageBytes + 1024 + 256;
 };
 
 template <int EPI>
@@ -127,6 +128,144 @@ W2V_DEV void epilogue_chunk(const GemmParams& p, long long out_row, long long re
     }
 }
 
+// ── coalesced epilogue ──────────────────────────────────────────────────────
+// tcgen05.ld 32x32b gives a thread one row; storing that directly makes each
+// warp instruction touch 32 rows.  Instead each epilogue warp stages its
+// 32 x 32 fp32 chunk in a private 4 KB shared buffer (float4 groups XOR-
+// swizzled by row, so the row-per-thread writes and the 8-threads-per-row
+// reads are both bank-conflict free) and then works on 4 rows x 32 columns
+// per instruction: thread t owns column group t%8 of rows t/8 + 4i.
+
+W2V_DEV void stage_put(float* stg, const float (&v)[32]) {
+    const int lane = threadIdx.x & 31;
+    float4* row = reinterpret_cast<float4*>(stg + lane * 32);
+#pragma unroll
+    for (int j = 0; j < 8; j++) row[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+W2V_DEV float4 stage_get(const float* stg, int r, int cg) {
+    return reinterpret_cast<const float4*>(stg + r * 32)[cg ^ (r & 7)];
+}
+
+// Residual of this thread's 8 (row, 4-column) cells of a chunk; rows past
+// m_valid and columns past N read as zero.
+W2V_DEV void load_resid_t(const GemmParams& p, long long out_row0, int row0, int col0, float4 (&res)[8]) {
+    const int lane = threadIdx.x & 31, cg = lane & 7, rs = lane >> 3;
+    const int col = col0 + 4 * cg;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int r = rs + 4 * i;
+        res[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row0 + r < p.m_valid) {
+            const float* src = p.resid + (out_row0 + r) * p.ldr + col;
+            if (col + 3 < p.N) res[i] = *reinterpret_cast<const float4*>(src);
+            else {
+                if (col < p.N) res[i].x = src[0];
+                if (col + 1 < p.N) res[i].y = src[1];
+                if (col + 2 < p.N) res[i].z = src[2];
+            }
+        }
+    }
+}
+
+template <int EPI>
+W2V_DEV void epilogue_chunk_t(const GemmParams& p, const float* stg, long long out_row0, int row0, int col0,
+                              const float4 (&res)[8]) {
+    const int lane = threadIdx.x & 31, cg = lane & 7, rs = lane >> 3;
+    const int col = col0 + 4 * cg;
+    if (col >= p.N) return;
+    const bool full4 = col + 3 < p.N;
+    float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p.bias) {
+        if (full4) b = __ldg(reinterpret_cast<const float4*>(p.bias + col));
+        else {
+            b.x = __ldg(p.bias + col);
+            if (col + 1 < p.N) b.y = __ldg(p.bias + col + 1);
+            if (col + 2 < p.N) b.z = __ldg(p.bias + col + 2);
+        }
+    }
+    // all shared-memory reads before any global store (which the compiler
+    // cannot prove disjoint from them), so the 32 cells compute in parallel
+    float4 xs[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) xs[i] = stage_get(stg, rs + 4 * i, cg);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float4& x = xs[i];
+        x.x += b.x; x.y += b.y; x.z += b.z; x.w += b.w;
+        if (EPI == W2V_EPI_F16_GELU) {
+            x.x = gelu_tanh(x.x); x.y = gelu_tanh(x.y); x.z = gelu_tanh(x.z); x.w = gelu_tanh(x.w);
+        }
+        if (EPI == W2V_EPI_F32_RESID) {
+            x.x += res[i].x; x.y += res[i].y; x.z += res[i].z; x.w += res[i].w;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int r = rs + 4 * i;
+        if (row0 + r >= p.m_valid) continue;
+        const float4 x = xs[i];
+        const long long orow = out_row0 + r;
+        if (EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU) {
+            __half* c = reinterpret_cast<__half*>(p.C) + orow * p.ldc + col;
+            if (full4) {
+                uint2 u;
+                u.x = pack_half2(x.x, x.y);
+                u.y = pack_half2(x.z, x.w);
+                *reinterpret_cast<uint2*>(c) = u;
+            } else {
+                c[0] = __float2half_rn(x.x);
+                if (col + 1 < p.N) c[1] = __float2half_rn(x.y);
+                if (col + 2 < p.N) c[2] = __float2half_rn(x.z);
+            }
+        } else {
+            float* c = reinterpret_cast<float*>(p.C) + orow * p.ldc + col;
+            if (full4) *reinterpret_cast<float4*>(c) = x;
+            else {
+                c[0] = x.x;
+                if (col + 1 < p.N) c[1] = x.y;
+                if (col + 2 < p.N) c[2] = x.z;
+            }
+        }
+    }
+}
+
+// One epilogue warp's share of an accumulator: TMEM lane quarter q (rows
+// row0 .. row0+31 of the batch), 32-column chunks c0 .. c1-1.
+template <int EPI>
+W2V_DEV void epilogue_warp(const GemmParams& p, uint32_t tmem_row, float* stg, long long out_row0, int row0,
+                           int col_base, int c0, int c1, float4 (&res)[8]) {
+    const int lane = threadIdx.x & 31;
+    if (!p.vec) {
+        // unaligned C or residual: row-per-thread scalar path
+        const bool valid = row0 + lane < p.m_valid;
+#pragma unroll 1
+        for (int c = c0; c < c1; c++) {
+            float v[32];
+            tmem_ld32(tmem_row + (uint32_t)(c * 32), v);
+            const int col0 = col_base + c * 32;
+            if (valid && col0 < p.N) epilogue_chunk<EPI>(p, out_row0 + lane, out_row0 + lane, col0, v);
+        }
+        return;
+    }
+#pragma unroll 1
+    for (int c = c0; c < c1; c++) {
+        float v[32];
+        tmem_ld32(tmem_row + (uint32_t)(c * 32), v);
+        const int col0 = col_base + c * 32;
+        float4 cur[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) cur[i] = res[i];
+        // next chunk's residual loads are in flight while this chunk is stored
+        if (EPI == W2V_EPI_F32_RESID && c + 1 < c1 && col0 + 32 < p.N) load_resid_t(p, out_row0, row0, col0 + 32, res);
+        __syncwarp();
+        stage_put(stg, v);
+        __syncwarp();
+        epilogue_chunk_t<EPI>(p, stg, out_row0, row0, col0, cur);
+    }
+    __syncwarp();
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
@@ -137,7 +276,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     uint8_t* sA = smem;
     uint8_t* sB = smem + S * Cfg::kABytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+    float* stage_buf = reinterpret_cast<float*>(sB + S * Cfg::kBBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes + kStageBytes);
     uint64_t* full = bars;
     uint64_t* empty = bars + S;
     uint64_t* tfull = bars + 2 * S;
@@ -219,7 +359,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
         const int half = (warp - 2) >> 2;       // which half of the tile's columns
         constexpr int kChunks = BN / 32 / 2;    // 32-column chunks per warp
-        const int r_in_tile = q * 32 + lane;
+        float* stg = stage_buf + (warp - 2) * 32 * 32;
         int it = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, it++) {
             const int ni = tile % p.n_tiles;
@@ -227,18 +367,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const int mi = rest % p.m_tiles, b = rest / p.m_tiles;
             const int ab = it & 1;
             const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+            const int row0 = mi * kBM + q * 32;
+            const long long out_row0 = (long long)b * p.c_batch_rows + row0;
+            const int c0 = half * kChunks;
+            float4 res[8];
+            // the residual does not depend on the MMA: fetch it while the MMA runs
+            if (EPI == W2V_EPI_F32_RESID && p.vec && ni * BN + c0 * 32 < p.N)
+                load_resid_t(p, out_row0, row0, ni * BN + c0 * 32, res);
             if (!mbar_wait(&tfull[ab], aph, p.err)) break;
             tc_fence_after();
-            const int row = mi * kBM + r_in_tile;
-            const bool valid = row < p.m_valid;
-            const long long out_row = (long long)b * p.c_batch_rows + row;
-#pragma unroll 1
-            for (int c = half * kChunks; c < (half + 1) * kChunks; c++) {
-                float v[32];
-                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN + c * 32), v);
-                const int col0 = ni * BN + c * 32;
-                if (valid && col0 < p.N) epilogue_chunk<EPI>(p, out_row, out_row, col0, v);
-            }
+            epilogue_warp<EPI>(p, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN), stg, out_row0, row0,
+                               ni * BN, c0, c0 + kChunks, res);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[ab]);
@@ -250,6 +389,177 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+// ── CTA-pair variant (tcgen05 cta_group::2) ─────────────────────────────────
+// A cluster of two CTAs computes a 256 x BN output tile.  Each CTA stages its
+// own 128 rows of A and BN/2 rows of B; the even CTA (the leader) issues
+// tcgen05.mma with M = 256, which reads the operands from both CTAs' shared
+// memory and writes rows 0..127 of the accumulator into the leader's TMEM and
+// rows 128..255 into the peer's.  Per SM this stages BN/2 instead of BN rows
+// of B for the same MMA work, cutting L2->SM operand traffic by a third at
+// BN = 256.
+//   full[s]   leader only: armed by the leader with both CTAs' bytes; both
+//             CTAs' TMA loads complete on it (peer through a cluster address)
+//   empty[s]  each CTA: the leader's MMA commit arrives on both
+//   tfull[b]  each CTA: accumulator b of this CTA's rows is ready
+//   tempty[b] leader: 16 epilogue warps (8 per CTA) have drained accumulator b
+//   done      leader: every MMA the leader issued has completed (teardown)
+template <int BN>
+struct Gemm2Cfg {
+    static constexpr int kABytes = kBM * kBK * 2;
+    static constexpr int kBBytes = (BN / 2) * kBK * 2;
+    static constexpr int kStages = BN == 256 ? 6 : 8;
+    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kSmem = kStages * (kABytes + kBBytes) + kStageBytes + 1024 + 256;
+};
+
+template <int BN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    using Cfg = Gemm2Cfg<BN>;
+    constexpr int S = Cfg::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    // identical offset in both CTAs: the MMA addresses the peer's operands
+    // at the leader's shared-memory offsets
+    uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + S * Cfg::kABytes;
+    float* stage_buf = reinterpret_cast<float*>(sB + S * Cfg::kBBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes + kStageBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + S;
+    uint64_t* tfull = bars + 2 * S;
+    uint64_t* tempty = bars + 2 * S + 2;
+    uint64_t* done = bars + 2 * S + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    const int total = p.n_batch * p.m_tiles * p.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 2 * kEpiWarps); }
+        mbar_init(done, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) { tmem_alloc_pair(tmem_slot, Cfg::kTmemCols); tmem_relinquish_pair(); }
+    tc_fence_before();
+    cluster_sync_all();    // barriers of both CTAs initialised before any cross-CTA signal
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            const uint32_t full_lead = mapa_shared(smem_u32(full), 0);
+            int stage = 0;
+            uint32_t phase = 0, issued = 0, last_par = 0;
+            bool ok = true;
+            for (int tile = pair; tile < total && ok; tile += n_pairs) {
+                const int ni = tile % p.n_tiles;
+                const int rest = tile / p.n_tiles;
+                const int mi = rest % p.m_tiles, b = rest / p.m_tiles;
+                const int row0 = (mi * 2 + (int)rank) * kBM;
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, p.err)) { ok = false; break; }
+                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (Cfg::kABytes + Cfg::kBBytes));
+                    const int tap = kb / p.kb_per_tap, cb = kb - tap * p.kb_per_tap;
+                    const uint32_t fb = full_lead + (uint32_t)(stage * 8);
+                    tma_load_4d_pair(sA + stage * Cfg::kABytes, &tmA, fb, cb * kBK, tap % p.conv_stride,
+                                     row0 + tap / p.conv_stride, b);
+                    tma_load_2d_pair(sB + stage * Cfg::kBBytes, &tmB, fb, kb * kBK, ni * BN + (int)rank * (BN / 2));
+                    issued |= 1u << stage;
+                    last_par = (last_par & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) { stage = 0; phase ^= 1u; }
+                }
+            }
+            // The leader's full barriers count both CTAs' bytes: once they
+            // have completed no bulk copy of the pair is still writing.  The
+            // peer leaves only after the closing cluster barrier, i.e. after
+            // this drain.
+            if (rank == 0)
+                for (int s = 0; s < S; s++)
+                    if (issued & (1u << s)) mbar_wait(&full[s], (last_par >> s) & 1u, p.err);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (rank == 0 && elect_one()) {
+            constexpr uint32_t idesc = umma_idesc_f16(2 * kBM, BN);
+            const uint32_t empty_peer = mapa_shared(smem_u32(empty), 1);
+            const uint32_t tfull_peer = mapa_shared(smem_u32(tfull), 1);
+            int stage = 0, it = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = pair; tile < total && ok; tile += n_pairs, it++) {
+                const int ab = it & 1;
+                const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+                if (!mbar_wait(&tempty[ab], aph ^ 1u, p.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(ab * BN);
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    if (!mbar_wait(&full[stage], phase, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * Cfg::kABytes);
+                    const uint32_t b0 = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / kUmmaK; kk++) {
+                        umma_f16_pair(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
+                                      (kb | kk) != 0);
+                    }
+                    umma_commit_pair(smem_u32(&empty[stage]));
+                    umma_commit_pair(empty_peer + (uint32_t)(stage * 8));
+                    if (++stage == S) { stage = 0; phase ^= 1u; }
+                }
+                if (ok) {
+                    umma_commit_pair(smem_u32(&tfull[ab]));
+                    umma_commit_pair(tfull_peer + (uint32_t)(ab * 8));
+                }
+            }
+            // no MMA may still be writing either CTA's TMEM at deallocation
+            umma_commit_pair(smem_u32(done));
+            mbar_wait(done, 0, p.err);
+        }
+        __syncwarp();
+    } else {
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        constexpr int kChunks = BN / 32 / 2;
+        const uint32_t tempty_lead = mapa_shared(smem_u32(tempty), 0);
+        float* stg = stage_buf + (warp - 2) * 32 * 32;
+        int it = 0;
+        for (int tile = pair; tile < total; tile += n_pairs, it++) {
+            const int ni = tile % p.n_tiles;
+            const int rest = tile / p.n_tiles;
+            const int mi = rest % p.m_tiles, b = rest / p.m_tiles;
+            const int ab = it & 1;
+            const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+            const int row0 = mi * 2 * kBM + (int)rank * kBM + q * 32;
+            const long long out_row0 = (long long)b * p.c_batch_rows + row0;
+            const int c0 = half * kChunks;
+            float4 res[8];
+            if (EPI == W2V_EPI_F32_RESID && p.vec && ni * BN + c0 * 32 < p.N)
+                load_resid_t(p, out_row0, row0, ni * BN + c0 * 32, res);
+            if (!mbar_wait(&tfull[ab], aph, p.err)) break;
+            tc_fence_after();
+            epilogue_warp<EPI>(p, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN), stg, out_row0, row0,
+                               ni * BN, c0, c0 + kChunks, res);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_lead + (uint32_t)(ab * 8));
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
     }
 }
 
@@ -321,28 +631,80 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPar
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
+// Clusters of two that can be resident at once (a GPC may leave an SM unpaired).
+template <int BN, int EPI>
+static int max_pairs(int dev) {
+    static int n[64] = {};
+    if (!n[dev & 63]) {
+        using Cfg = Gemm2Cfg<BN>;
+        auto kern = gemm2_tc_kernel<BN, EPI>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) != cudaSuccess)
+            return 0;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = Cfg::kSmem;
+        int c = 0;
+        if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) != cudaSuccess || c <= 0) {
+            cudaGetLastError();
+            c = sm_count() / 2;
+        }
+        n[dev & 63] = c;
+    }
+    return n[dev & 63];
+}
+
+template <int BN, int EPI>
+static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
+    using Cfg = Gemm2Cfg<BN>;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int mp = max_pairs<BN, EPI>(dev);
+    if (mp <= 0) return W2V_ERR_LAUNCH;
+    const int total = p.n_batch * p.m_tiles * p.n_tiles;
+    const int pairs = total < mp ? total : mp;
+    gemm2_tc_kernel<BN, EPI><<<2 * pairs, kThreads, Cfg::kSmem, st>>>(ta, tb, p);
+    return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
+}
+
 template <int EPI>
 static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
     switch (bn) {
         case 256: return launch_bn<256, EPI>(ta, tb, p, st);
         case 128: return launch_bn<128, EPI>(ta, tb, p, st);
+        case -256: return launch_pair<256, EPI>(ta, tb, p, st);
+        case -128: return launch_pair<128, EPI>(ta, tb, p, st);
         default: return launch_bn<64, EPI>(ta, tb, p, st);
     }
 }
 
-// Pick the N tile: the widest of 256/128/64 dividing N (64 covers small or
-// ragged N through TMA zero fill), preferring fewer wasted wave slots.
-static int pick_bn(int N, long long m_tiles_total) {
+// Pick the tile: single-CTA 128 x {256,128,64} (64 covers small or ragged N
+// through TMA zero fill) or CTA-pair 256 x {256,128} (returned negated).
+// Estimated time = waves x tile width x (K x m + E x e):
+//   m  MMA time per unit of K relative to 128 x 256 tiles (narrow tiles stage
+//      more operand bytes per MAC; pairs stage half of B per SM);
+//   E  epilogue work per output in the same units (fp16 store < fp32 store <
+//      GELU < fp32 residual), only partly hidden behind the next tile's MMAs;
+//   e  pairs wait for both CTAs' epilogues before reusing an accumulator.
+// Constants fitted on B200 to the encoder GEMMs (M = 31936, K = 768/3072,
+// N = 768/2304/3072, every epilogue), within about 5 % of measured times.
+static int pick_bn(int N, int m_valid, int n_batch, long long K, int epilogue) {
     const int sms = sm_count();
+    const long long mt1 = (long long)((m_valid + kBM - 1) / kBM) * n_batch;
+    const long long mt2 = (long long)((m_valid + 2 * kBM - 1) / (2 * kBM)) * n_batch;
+    const double E = epilogue == W2V_EPI_F16 ? 293 : epilogue == W2V_EPI_F16_GELU ? 589
+                   : epilogue == W2V_EPI_F32 ? 450 : 932;
     int best = 64;
-    double best_cost = 1e30;
-    for (int bn : {256, 128, 64}) {
-        if (N % bn != 0 && bn != 64) continue;
-        const long long tiles = m_tiles_total * ((N + bn - 1) / bn);
-        const long long waves = (tiles + sms - 1) / sms;
-        // time ~ waves * per-tile time (proportional to bn), plus a small
-        // penalty for narrower tiles (more A re-reads, less MMA efficiency)
-        const double cost = (double)waves * bn * (bn == 64 ? 1.15 : (bn == 128 ? 1.05 : 1.0));
+    double best_cost = 1e300;
+    for (int bn : {256, 128, 64, -256, -128}) {
+        const int w = bn < 0 ? -bn : bn;
+        if (N % w != 0 && bn != 64) continue;
+        const long long tiles = (bn < 0 ? mt2 : mt1) * ((N + w - 1) / w);
+        const long long slots = bn < 0 ? sms / 2 : sms;
+        const long long waves = (tiles + slots - 1) / slots;
+        const double m = bn == 256 ? 1.0 : bn == 128 ? 1.3 : bn == 64 ? 1.6 : bn == -256 ? 0.78 : 1.3;
+        const double e = bn < 0 ? 1.34 : 1.0;
+        const double cost = (double)waves * w * ((double)K * m + E * e);
         if (cost < best_cost) { best_cost = cost; best = bn; }
     }
     return best;
@@ -388,12 +750,13 @@ extern "C" int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_st
     p.kb_per_tap = (int)(a_cin / kBK);
     p.conv_stride = a_stride;
     p.m_valid = m_valid;
-    p.m_tiles = (int)((m_valid + kBM - 1) / kBM);
     p.n_batch = (int)a_batches;
     p.N = N;
-    int bn = block_n ? block_n : pick_bn(N, (long long)p.m_tiles * p.n_batch);
-    if (bn != 256 && bn != 128 && bn != 64) return W2V_ERR_ARGS;
-    p.n_tiles = (N + bn - 1) / bn;
+    const int bn = block_n ? block_n : pick_bn(N, m_valid, p.n_batch, K, epilogue);
+    if (bn != 256 && bn != 128 && bn != 64 && bn != -256 && bn != -128) return W2V_ERR_ARGS;
+    const int tile_rows = bn < 0 ? 2 * kBM : kBM, tile_cols = bn < 0 ? -bn : bn;
+    p.m_tiles = (int)((m_valid + tile_rows - 1) / tile_rows);
+    p.n_tiles = (N + tile_cols - 1) / tile_cols;
     p.k_blocks = (int)(K / kBK);
     p.C = C;
     p.ldc = ldc;
@@ -411,7 +774,7 @@ extern "C" int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_st
     }
     const uint64_t bdims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t bstr[1] = {(uint64_t)K * 2};
-    const uint32_t bbox[2] = {kBK, (uint32_t)bn};
+    const uint32_t bbox[2] = {kBK, (uint32_t)(bn < 0 ? -bn / 2 : bn)};
     rc = make_map_f16(&tb, B, 2, bdims, bstr, bbox);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
