@@ -49,8 +49,8 @@ enum {
  *   B: fp16 [N, K] row-major.
  *   C: row (b, r) at C + (b*c_batch_rows + r)*ldc, written for r < m_valid.
  *   bias: fp32 [N] or NULL; resid: fp32 rows like C (ldr), may alias C.
- *   block_n: 0 = automatic; 64/128/256 = one CTA per 128 x block_n tile;
- *            -128/-256 = a CTA pair (tcgen05 cta_group::2) per 256 x -block_n tile. */
+ *   block_n: 0 = automatic; 64/128/192/256 = one CTA per 128 x block_n tile;
+ *            -128/-192/-256 = a CTA pair (tcgen05 cta_group::2) per 256 x -block_n tile. */
 int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_stride, long long a_row_stride,
                  long long a_rows_in, long long a_batches, long long a_batch_stride, const void* B,
                  int N, void* C, long long ldc, long long c_batch_rows, int m_valid, const float* bias,

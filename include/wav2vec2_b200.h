@@ -20,6 +20,7 @@ enum {
     W2V_STATUS_CUDA = 2,      /* CUDA runtime or kernel launch error */
     W2V_STATUS_DEVICE = 3,    /* a kernel reported a device-side error */
     W2V_STATUS_MODEL = 4,     /* model file missing, corrupt or unsupported */
+    W2V_STATUS_AUDIO = 5,     /* audio file missing, malformed or unsupported */
 };
 
 /* Message of the most recent failure on this thread ("" if none). */
@@ -90,6 +91,15 @@ int wav2vec2_b200_profile_read(struct wav2vec2_context * ctx, const char ** name
 
 /* Kernel launches of the most recent forward on the first device. */
 long long wav2vec2_b200_launches_per_forward(const struct wav2vec2_context * ctx);
+
+/* Read a WAV file as mono float samples at target_sr Hz (<= 0: 16000): PCM
+ * 16-bit, PCM 32-bit or float 32-bit, any channel count (averaged) and rate
+ * (linear interpolation).  Same decoding, messages and results as the
+ * reference CLI's reader (examples/main/main.cpp:20-82), which has no library
+ * counterpart.  *samples is malloc'd (free with wav2vec2_b200_free_samples;
+ * NULL when *n_samples is 0).  Returns W2V_STATUS_AUDIO on a bad file. */
+int wav2vec2_b200_load_wav(const char * path, int target_sr, float ** samples, int * n_samples);
+void wav2vec2_b200_free_samples(float * samples);
 
 #ifdef __cplusplus
 }

@@ -224,6 +224,24 @@ def quantize_q8_0_rows(x):
     return out
 
 
+def ref_load_wav(path, target_sr: int = 16000, cap: int | None = None):
+    """The reference CLI's WAV reader (examples/main/main.cpp:20-82), compiled
+    from its source.  Returns float32 samples, or raises RuntimeError with the
+    reference's message.  The reader loops forever on a file with no "data"
+    chunk (its chunk loop seeks, which clears end-of-file), so callers must
+    not pass one."""
+    if cap is None:
+        cap = max(1 << 16, 8 * os.path.getsize(path) * max(1, target_sr // 8000))
+    out = np.empty(cap, np.float32)
+    err = ctypes.create_string_buffer(512)
+    n = RefOracle.lib().w2vref_load_wav(str(path).encode(), target_sr, out.ctypes.data, cap, err, 512)
+    if n == -1:
+        raise RuntimeError(err.value.decode())
+    if n < 0:
+        raise RuntimeError("capacity")
+    return out[:n].copy()
+
+
 class RefOracle(_Base):
     """The reference's own sources (oracle/_ref/libw2v_ref.so)."""
     _lib = None
@@ -251,6 +269,9 @@ class RefOracle(_Base):
             L.w2vref_layer_norm.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int]
             L.w2vref_group_norm.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int]
             L.w2vref_softmax.argtypes = [_vp, ctypes.c_int]
+            L.w2vref_load_wav.restype = ctypes.c_long
+            L.w2vref_load_wav.argtypes = [ctypes.c_char_p, ctypes.c_int, _vp, ctypes.c_long, ctypes.c_char_p,
+                                          ctypes.c_int]
             cls._lib = L
         return cls._lib
 

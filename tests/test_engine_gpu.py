@@ -137,6 +137,38 @@ def test_beam_search_matches_reference_decoder(W, model_path, synth):
         assert m.transcribe(x, beam_size=5)["text"] == text
 
 
+def test_batched_beam_overlaps_batches(W, model_path, synth):
+    """Beam search through wav2vec2_transcribe_batch with several device
+    batches (max_batch 2): the host decoding pool must give, in input order,
+    the reference decoder's result on each utterance's GPU logits."""
+    p = model_path("tiny_pre", "q4_0", bias_std=0.02, gain_jitter=0.1)
+    m = W.Model(p, max_batch=2)
+    toks = synth.vocab_tokens(m.cfg["vocab"])
+    lens = [16000, 7000, 12000, 3000, 9000, 16000, 400]
+    xs = [synth.make_audio(n, 80 + i) for i, n in enumerate(lens)]
+    got = m.transcribe_batch(xs, beam_size=4, n_threads=3)
+    for x, r in zip(xs, got):
+        ids = O.ref_beam_search(m.logits([x])[0], 0, 4)
+        text = "".join(" " if toks[j] == "|" else ("" if toks[j].startswith("<") else toks[j]) for j in ids).strip()
+        assert r["text"] == text and not r["words"]
+
+
+def test_wav_file_transcribes_like_array(W, model_path, synth, tmp_path):
+    """Audio ingestion feeding the engine: a 44.1 kHz stereo PCM16 file,
+    decoded by wav2vec2_b200_load_wav, transcribes exactly like the decoded
+    samples passed directly."""
+    p = model_path("tiny", "q8_0")
+    m = model(W, p)
+    x = synth.make_audio(44100, 7)
+    st = np.stack([x, 0.5 * x[::-1]], 1)
+    f = tmp_path / "a.wav"
+    f.write_bytes(synth.wav_bytes(st, 44100, "pcm16"))
+    a = W.load_wav(f)
+    assert a.dtype == np.float32 and len(a) == 16000
+    assert m.transcribe_batch([a])[0]["text"] == m.transcribe(a)["text"]
+    assert np.array_equal(m.logits([a])[0], m.logits([W.load_wav(f)])[0])
+
+
 class _DevArray:
     """Wrap a raw device pointer for torch.as_tensor (CUDA array interface)."""
 

@@ -78,7 +78,8 @@ def test_gemm_plain(K, M, N, Kd, epi, bn):
     (1, 256, 64, EPI_F32, -256), (255, 256, 768, EPI_F16, -256), (257, 512, 768, EPI_F32_RESID, -256),
     (20000, 2304, 768, EPI_F16, -256), (9000, 768, 3072, EPI_F32_RESID, -256), (7777, 3072, 768, EPI_F16_GELU, -256),
     (9000, 768, 768, EPI_F32_RESID, -128), (300, 200, 512, EPI_F32, -256), (513, 96, 256, EPI_F16, -128),
-    (4000, 1280, 1280, EPI_F16_GELU, -128)])
+    (4000, 1280, 1280, EPI_F16_GELU, -128), (9000, 768, 3072, EPI_F32_RESID, -192),
+    (5000, 768, 768, EPI_F32_RESID, 192), (777, 200, 512, EPI_F16_GELU, 192), (300, 500, 256, EPI_F16, -192)])
 def test_gemm_cta_pair(K, M, N, Kd, epi, bn):
     """CTA-pair (cta_group::2) tiles of 256 x |bn|: ragged M and N, several
     tiles per pair (both TMEM accumulators in turn), every epilogue."""
@@ -107,7 +108,7 @@ def test_gemm_cta_pair(K, M, N, Kd, epi, bn):
 
 
 @pytest.mark.parametrize("epi", [EPI_F16_GELU, EPI_F32_RESID])
-@pytest.mark.parametrize("bn", [0, 128, -256])
+@pytest.mark.parametrize("bn", [0, 128, 192, -256, -192])
 def test_gemm_ragged_columns(K, epi, bn):
     """N not a multiple of 4 inside a wider row pitch: the last column group
     of each row is stored element by element, columns N..ldc-1 untouched."""

@@ -54,6 +54,8 @@ SIGNATURES = {
     "wav2vec2_b200_profile": (_i, [_vp, _i]),
     "wav2vec2_b200_profile_read": (_i, [_vp, _vp, _vp, _vp, _vp, _i]),
     "wav2vec2_b200_launches_per_forward": (_ll, [_vp]),
+    "wav2vec2_b200_load_wav": (_i, [C.c_char_p, _i, _vp, _vp]),
+    "wav2vec2_b200_free_samples": (None, [_vp]),
     # kernel layer (include/w2v_kernels.h)
     "w2v_gemm_f16": (_i, [_vp, _ll, _i, _i, _ll, _ll, _ll, _ll, _vp, _i, _vp, _ll, _ll, _i, _vp, _vp, _ll, _i,
                           _i, _vp, _vp]),
@@ -103,6 +105,22 @@ def _ptr_array(arrs):
 
 class EngineError(RuntimeError):
     pass
+
+
+def load_wav(path: str | Path, target_sr: int = 16000) -> np.ndarray:
+    """Mono float32 samples at target_sr from a WAV file
+    (wav2vec2_b200_load_wav; the reference CLI's decoding)."""
+    p = C.c_void_p()
+    n = C.c_int()
+    rc = lib().wav2vec2_b200_load_wav(str(path).encode(), target_sr, C.byref(p), C.byref(n))
+    if rc != 0:
+        raise EngineError(last_error())
+    try:
+        if n.value == 0:
+            return np.zeros(0, np.float32)
+        return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_float)), shape=(n.value,)).copy()
+    finally:
+        lib().wav2vec2_b200_free_samples(p)
 
 
 class Model:

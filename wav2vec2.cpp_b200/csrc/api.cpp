@@ -13,7 +13,11 @@
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <condition_variable>
 #include <cstring>
+#include <deque>
+#include <exception>
+#include <functional>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -23,6 +27,7 @@
 
 #include "engine.hpp"
 #include "shard.hpp"
+#include "audio.hpp"
 #include "wav2vec2_b200.h"
 
 using namespace w2v;
@@ -182,10 +187,76 @@ wav2vec2_result* make_result(const ModelConfig& c, int T, const std::string& tex
     return r;
 }
 
+// Host decoding pool: device workers hand each finished batch's utterances
+// to it and go straight on to their next batch, so prefix beam search (the
+// reference's host decoder, src/ops.h:151-251) overlaps the GPU forward of
+// the following batches.  finish() drains the queue, joins and rethrows the
+// first task failure; the destructor (an error path) drains and joins only.
+class DecodePool {
+public:
+    explicit DecodePool(int n) {
+        for (int i = 0; i < n; i++) th_.emplace_back([this] { loop(); });
+    }
+    ~DecodePool() { join(); }
+    void push(std::function<void()> f) {
+        {
+            std::lock_guard<std::mutex> l(m_);
+            q_.push_back(std::move(f));
+        }
+        cv_.notify_one();
+    }
+    // Wait for every queued task; rethrows the first task exception.
+    void finish() {
+        join();
+        if (err_) {
+            auto e = err_;
+            err_ = nullptr;
+            std::rethrow_exception(e);
+        }
+    }
+
+private:
+    void join() {
+        {
+            std::lock_guard<std::mutex> l(m_);
+            done_ = true;
+        }
+        cv_.notify_all();
+        for (auto& t : th_)
+            if (t.joinable()) t.join();
+        th_.clear();
+    }
+    void loop() {
+        for (;;) {
+            std::function<void()> f;
+            {
+                std::unique_lock<std::mutex> l(m_);
+                cv_.wait(l, [this] { return done_ || !q_.empty(); });
+                if (q_.empty()) return;
+                f = std::move(q_.front());
+                q_.pop_front();
+            }
+            try {
+                f();
+            } catch (...) {
+                std::lock_guard<std::mutex> l(m_);
+                if (!err_) err_ = std::current_exception();
+            }
+        }
+    }
+    std::vector<std::thread> th_;
+    std::deque<std::function<void()>> q_;
+    std::mutex m_;
+    std::condition_variable cv_;
+    bool done_ = false;
+    std::exception_ptr err_;
+};
+
 // Run every batch, sharded over the context's devices (shard.hpp: one host
 // thread per device pulling from a shared queue; a failing device retires and
 // its batch is re-queued); fn(engine, batch index list, logits, spans,
-// n_spans, geometry) consumes each result on the worker thread.
+// n_spans, geometry) consumes each result on the worker thread (it may move
+// the logits out).
 template <typename Fn>
 void run_sharded(wav2vec2_context* ctx, const float* const* samples, const int* n_samples, int n_utt,
                  bool want_logits, bool want_spans, Fn fn) {
@@ -301,44 +372,45 @@ int wav2vec2_transcribe_batch(wav2vec2_context* ctx, wav2vec2_params params, con
     const ModelConfig& c = ctx->cfg;
     const bool beam = params.beam_size > 1;
     try {
+        // beam: decoded by a host pool overlapping later batches' GPU work;
+        // greedy: spans come from the GPU, detokenised inline
+        std::unique_ptr<DecodePool> pool;
+        if (beam) pool.reset(new DecodePool(std::max(1, params.n_threads)));
         run_sharded(ctx, samples, n_samples, n_utt, beam, !beam,
-                    [&](Engine*, const std::vector<int>& b, const std::vector<float>& logits,
+                    [&](Engine*, const std::vector<int>& b, std::vector<float>& logits,
                         const std::vector<int>& spans, const std::vector<int>& nsp, const BatchGeom& g) {
-                        // host decoding of this batch with up to n_threads threads
                         const int nb = (int)b.size();
-                        auto decode = [&](int j) {
-                            const int T = g.T[j];
-                            std::vector<Word> words;
-                            std::string text;
-                            if (beam) {
-                                const float* lg = logits.data() + (size_t)g.T_off[j] * c.vocab;
-                                text = ids_to_text(beam_search(lg, T, c.vocab, c.pad_id, params.beam_size), c);
-                            } else {
-                                std::vector<Span> sp;
-                                std::vector<int> ids;
-                                for (int k = 0; k < (T > 0 ? nsp[j] : 0); k++) {
-                                    const int* s = spans.data() + 3 * ((size_t)g.T_off[j] + k);
-                                    sp.push_back({s[0], s[1], s[2]});
-                                    if (s[0] != c.pad_id) ids.push_back(s[0]);
-                                }
-                                text = ids_to_text(ids, c);
-                                if (params.word_timestamps) words = spans_to_words(sp, c);
-                            }
-                            results[b[j]] = make_result(c, T, text, params.word_timestamps ? &words : nullptr);
-                        };
-                        const int nt = std::max(1, std::min(params.n_threads, nb));
-                        if (nt == 1 || !beam) {
-                            for (int j = 0; j < nb; j++) decode(j);
-                        } else {
-                            std::atomic<int> nx{0};
-                            std::vector<std::thread> th;
-                            for (int t = 0; t < nt; t++)
-                                th.emplace_back([&]() {
-                                    for (int j; (j = nx.fetch_add(1)) < nb;) decode(j);
+                        if (beam) {
+                            auto lg = std::make_shared<std::vector<float>>(std::move(logits));
+                            auto geo = std::make_shared<BatchGeom>(g);
+                            for (int j = 0; j < nb; j++) {
+                                const int u = b[j];
+                                pool->push([&, lg, geo, j, u] {
+                                    const int T = geo->T[j];
+                                    const float* l = lg->data() + (size_t)geo->T_off[j] * c.vocab;
+                                    const std::string text =
+                                        ids_to_text(beam_search(l, T, c.vocab, c.pad_id, params.beam_size), c);
+                                    results[u] = make_result(c, T, text, nullptr);
                                 });
-                            for (auto& t : th) t.join();
+                            }
+                            return;
+                        }
+                        for (int j = 0; j < nb; j++) {
+                            const int T = g.T[j];
+                            std::vector<Span> sp;
+                            std::vector<int> ids;
+                            for (int k = 0; k < (T > 0 ? nsp[j] : 0); k++) {
+                                const int* s = spans.data() + 3 * ((size_t)g.T_off[j] + k);
+                                sp.push_back({s[0], s[1], s[2]});
+                                if (s[0] != c.pad_id) ids.push_back(s[0]);
+                            }
+                            std::vector<Word> words;
+                            if (params.word_timestamps) words = spans_to_words(sp, c);
+                            results[b[j]] = make_result(c, T, ids_to_text(ids, c),
+                                                        params.word_timestamps ? &words : nullptr);
                         }
                     });
+        if (pool) pool->finish();
     } catch (const std::exception& e) {
         for (int i = 0; i < n_utt; i++) { wav2vec2_result_free(results[i]); results[i] = nullptr; }
         set_error(e.what());
@@ -472,5 +544,31 @@ int wav2vec2_b200_profile_read(wav2vec2_context* ctx, const char** names, double
 long long wav2vec2_b200_launches_per_forward(const wav2vec2_context* ctx) {
     return ctx ? ctx->engines[0]->launches_last_forward() : 0;
 }
+
+int wav2vec2_b200_load_wav(const char* path, int target_sr, float** samples, int* n_samples) {
+    if (!samples || !n_samples) {
+        set_error("invalid arguments");
+        return W2V_STATUS_INVALID;
+    }
+    *samples = nullptr;
+    *n_samples = 0;
+    try {
+        const std::vector<float> a = load_wav(path, target_sr > 0 ? target_sr : 16000);
+        if (a.size() > (size_t)0x7fffffff) throw std::runtime_error("WAV too long");
+        if (!a.empty()) {
+            float* out = static_cast<float*>(std::malloc(a.size() * sizeof(float)));
+            if (!out) throw std::runtime_error("out of host memory");
+            std::memcpy(out, a.data(), a.size() * sizeof(float));
+            *samples = out;
+        }
+        *n_samples = (int)a.size();
+        return W2V_STATUS_OK;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return W2V_STATUS_AUDIO;
+    }
+}
+
+void wav2vec2_b200_free_samples(float* samples) { std::free(samples); }
 
 }  // extern "C"

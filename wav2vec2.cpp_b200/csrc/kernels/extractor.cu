@@ -63,25 +63,157 @@ W2V_DEV T block_sum(T v, T* red) {
     return s;
 }
 
-__global__ void wave_stats_kernel(const float* __restrict__ audio, const long long* __restrict__ off,
-                                  const int* __restrict__ len, float* __restrict__ stats) {
+// One block per utterance, one pass: sum and sum of squares in fp64 (four
+// independent accumulators per thread, 16-byte loads on the aligned body).
+// var = E[x^2] - mean^2 in fp64 equals the reference's two-pass fp32
+// population variance to well below fp32 resolution for audio-range values.
+__global__ void __launch_bounds__(1024) wave_stats_kernel(const float* __restrict__ audio,
+                                                          const long long* __restrict__ off,
+                                                          const int* __restrict__ len, float* __restrict__ stats) {
     __shared__ double red[32];
     const int u = blockIdx.x;
     const float* x = audio + off[u];
     const int n = len[u];
-    double s = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
-    const double mean_d = block_sum(s, red) / n;
-    const float mean = (float)mean_d;
-    double v = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const double d = (double)(x[i] - mean);
-        v += d * d;
+    if (n <= 0) {
+        if (threadIdx.x == 0) { stats[2 * u] = 0.f; stats[2 * u + 1] = 1.f / sqrtf(1e-7f); }
+        return;
     }
-    const float var = (float)(block_sum(v, red) / n);
+    // scalar head up to a 16-byte boundary, float4 body, scalar tail
+    const int head = min(n, (int)(((16 - (reinterpret_cast<uintptr_t>(x) & 15)) & 15) / 4));
+    const int nv = (n - head) / 4;
+    const float4* xv = reinterpret_cast<const float4*>(x + head);
+    double s0 = 0, s1 = 0, q0 = 0, q1 = 0;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+        const float4 v = __ldg(xv + i);
+        s0 += (double)v.x + (double)v.y;
+        s1 += (double)v.z + (double)v.w;
+        q0 = fma((double)v.x, (double)v.x, fma((double)v.y, (double)v.y, q0));
+        q1 = fma((double)v.z, (double)v.z, fma((double)v.w, (double)v.w, q1));
+    }
+    for (int i = threadIdx.x; i < head; i += blockDim.x) { const double v = x[i]; s0 += v; q0 = fma(v, v, q0); }
+    for (int i = head + 4 * nv + threadIdx.x; i < n; i += blockDim.x) {
+        const double v = x[i];
+        s1 += v;
+        q1 = fma(v, v, q1);
+    }
+    const double S = block_sum(s0 + s1, red);
+    const double Q = block_sum(q0 + q1, red);
     if (threadIdx.x == 0) {
-        stats[2 * u] = mean;
+        const double mean = S / n;
+        const float var = (float)fmax(Q / n - mean * mean, 0.0);
+        stats[2 * u] = (float)mean;
         stats[2 * u + 1] = 1.f / sqrtf(var + 1e-7f);
+    }
+}
+
+// ── conv layer 0 GroupNorm statistics from window moments ───────────────────
+// For the published first layer (kernel 10, stride 5) with GroupNorm (one
+// group per channel, statistics over all frames; src/ops.h:39-50) the mean
+// and variance of y[f,c] = b[c] + sum_k w[c,k] xn[5f+k] over the F frames
+// follow exactly from the moments of the normalised windows xn = (x - mu) r:
+//   sum_f y   = F b + w.S
+//   sum_f y^2 = F b^2 + 2 b w.S + w^T G w,
+//   S_k = sum_f xn[5f+k],  G_kl = sum_f xn[5f+k] xn[5f+l].
+// S and G are accumulated in fp64 from the raw samples (a product of two
+// floats is exact in fp64) and normalised afterwards with the utterance's
+// (mu, r): 65 fp64 FMAs per frame instead of a second evaluation of the
+// 5120-FMA convolution.  Per-chunk partials are reduced in a fixed order, so
+// an utterance's statistics do not depend on the rest of its batch.
+constexpr int kGramK = 10, kGramS = 5, kGramN = kGramK + kGramK * (kGramK + 1) / 2;   // 65
+constexpr int kGramThreads = 256;
+
+W2V_DEV int gram_index(int k, int l) {   // k <= l
+    return kGramK + k * kGramK - k * (k - 1) / 2 + (l - k);
+}
+
+__global__ void __launch_bounds__(kGramThreads) conv0_gram_kernel(const float* __restrict__ audio,
+                                                                  const long long* __restrict__ off,
+                                                                  const int* __restrict__ frames, int chunks,
+                                                                  double* __restrict__ part) {
+    __shared__ double red[kGramThreads / 32][kGramN];
+    const int u = blockIdx.y, ch = blockIdx.x;
+    const int F = frames[u];
+    const int per = (F + chunks - 1) / chunks;
+    const int f0 = ch * per, f1 = min(F, f0 + per);
+    const float* x = audio + off[u];
+    double acc[kGramN];
+#pragma unroll
+    for (int i = 0; i < kGramN; i++) acc[i] = 0.0;
+    for (int f = f0 + (int)threadIdx.x; f < f1; f += kGramThreads) {
+        double v[kGramK];
+#pragma unroll
+        for (int k = 0; k < kGramK; k++) v[k] = (double)__ldg(x + (long long)f * kGramS + k);
+#pragma unroll
+        for (int k = 0; k < kGramK; k++) {
+            acc[k] += v[k];
+#pragma unroll
+            for (int l = k; l < kGramK; l++) acc[gram_index(k, l)] = fma(v[k], v[l], acc[gram_index(k, l)]);
+        }
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < kGramN; i++) {
+        double a = acc[i];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) red[w][i] = a;
+    }
+    __syncthreads();
+    if (threadIdx.x < kGramN) {
+        double t = 0.0;
+#pragma unroll
+        for (int i = 0; i < kGramThreads / 32; i++) t += red[i][threadIdx.x];
+        part[((long long)u * chunks + ch) * kGramN + threadIdx.x] = t;
+    }
+}
+
+// Per (utterance, channel) GroupNorm mean and 1/sqrt(var + 1e-5) from the
+// window moments; `stats` holds the (mu, r) the conv kernel normalises with.
+__global__ void conv0_gram_finalize_kernel(const double* __restrict__ part, int chunks,
+                                           const float* __restrict__ stats, const int* __restrict__ frames,
+                                           const float* __restrict__ w0, const float* __restrict__ b0, int C,
+                                           float2* __restrict__ gnf) {
+    __shared__ double m[kGramN];
+    __shared__ double Sn[kGramK];
+    __shared__ double Gn[kGramK][kGramK];
+    const int u = blockIdx.x;
+    if (threadIdx.x < kGramN) {
+        double t = 0.0;
+        for (int c = 0; c < chunks; c++) t += part[((long long)u * chunks + c) * kGramN + threadIdx.x];
+        m[threadIdx.x] = t;
+    }
+    __syncthreads();
+    const int F = frames[u];
+    const double Fd = (double)F, mu = (double)stats[2 * u], r = (double)stats[2 * u + 1];
+    if (threadIdx.x < kGramK) Sn[threadIdx.x] = r * (m[threadIdx.x] - Fd * mu);
+    if (threadIdx.x < kGramK * kGramK) {
+        const int k = threadIdx.x / kGramK, l = threadIdx.x % kGramK;
+        const double P = m[gram_index(min(k, l), max(k, l))];
+        Gn[k][l] = r * r * (P - mu * (m[k] + m[l]) + Fd * mu * mu);
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float2 o = make_float2(0.f, 1.f / sqrtf(1e-5f));
+        if (F > 0) {
+            double wv[kGramK];
+#pragma unroll
+            for (int k = 0; k < kGramK; k++) wv[k] = (double)__ldg(w0 + c * kGramK + k);
+            const double b = b0 ? (double)__ldg(b0 + c) : 0.0;
+            double ws = 0.0, wgw = 0.0;
+#pragma unroll
+            for (int k = 0; k < kGramK; k++) {
+                ws = fma(wv[k], Sn[k], ws);
+                double g = 0.0;
+#pragma unroll
+                for (int l = 0; l < kGramK; l++) g = fma(wv[l], Gn[k][l], g);
+                wgw = fma(wv[k], g, wgw);
+            }
+            const double mean = (Fd * b + ws) / Fd;
+            const double ey2 = (Fd * b * b + 2.0 * b * ws + wgw) / Fd;
+            const float var = (float)fmax(ey2 - mean * mean, 0.0);
+            o = make_float2((float)mean, 1.f / sqrtf(var + 1e-5f));
+        }
+        gnf[(long long)u * C + c] = o;
     }
 }
 
@@ -101,6 +233,7 @@ struct Conv0Args {
     const float* audio; const long long* off; const int* len; const int* frames;
     const float* stats; const float* w0; const float* b0; int C, k0, s0, norm;
     const float* gw; const float* gb; double* gn; __half* out; long long rows_max;
+    const float2* gnf;   // GroupNorm (mean, 1/std) per (utterance, channel), when precomputed
 };
 
 // Stage normalised samples for frames f0 .. f0+nf-1 (zero-padded by kC0MaxK).
@@ -404,7 +537,14 @@ __global__ void __launch_bounds__(128) conv0x4_apply_kernel(Conv0Args a) {
 #pragma unroll
             for (int c = 0; c < 4; c++) { ga[c] = a.gw[c0 + c]; be[c] = a.gb[c0 + c]; }
         }
-        if (a.norm == 1) {
+        if (a.norm == 1 && a.gnf) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float2 g = a.gnf[(long long)u * a.C + c0 + c];
+                m[c] = g.x;
+                iv[c] = g.y;
+            }
+        } else if (a.norm == 1) {
             const double* gp = a.gn + ((long long)u * a.C + c0) * 2;
 #pragma unroll
             for (int c = 0; c < 4; c++) {
@@ -628,7 +768,7 @@ extern "C" int w2v_dequant_f16(const void* raw, int type, long long n_rows, long
 extern "C" int w2v_wave_stats(const float* audio, const long long* off, const int* len, int n_utt, float* stats,
                               void* stream) {
     if (n_utt <= 0) return W2V_OK;
-    wave_stats_kernel<<<n_utt, 512, 0, S(stream)>>>(audio, off, len, stats);
+    wave_stats_kernel<<<n_utt, 1024, 0, S(stream)>>>(audio, off, len, stats);
     return launch_rc();
 }
 
@@ -639,18 +779,37 @@ extern "C" int w2v_conv0(const float* audio, const long long* off, const int* le
     if (C > 512 || C % 2 || k0 > kC0MaxK || k0 <= 0 || s0 <= 0 || norm < 0 || norm > 2) return W2V_ERR_ARGS;
     if ((norm == 1 && !gn_sums) || (norm && (!gw || !gb))) return W2V_ERR_ARGS;
     if (n_utt <= 0 || max_frames <= 0) return W2V_OK;
-    Conv0Args a{audio, off, len, frames, stats, w0, b0, C, k0, s0, norm, gw, gb, gn_sums, (__half*)out, rows_max};
+    Conv0Args a{audio, off, len, frames, stats, w0, b0, C, k0, s0, norm, gw, gb, gn_sums, (__half*)out, rows_max,
+                nullptr};
     const bool k10 = k0 == 10;
     if (k0 == kC0K && s0 == kC0S && C % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0) {
         // published shape: 4 channels per thread, 8-frame register windows
         if (norm == 1) {
-            if (cudaMemsetAsync(gn_sums, 0, sizeof(double) * 2 * C * (size_t)n_utt, S(stream)) != cudaSuccess)
-                return W2V_ERR_LAUNCH;
-            const size_t sh = (size_t)((kC0StatFrames - 1) * s0 + k0 + kC0MaxK + kC0Win) * sizeof(float);
-            dim3 g((max_frames + kC0StatFrames - 1) / kC0StatFrames, n_utt);
-            conv0x4_gn_stats_kernel<<<g, 128, sh, S(stream)>>>(a);
-            int rc = launch_rc();
-            if (rc) return rc;
+            // GroupNorm statistics from fp64 window moments.  gn_sums
+            // ([n_utt][C][2] doubles) holds the (mean, 1/std) floats in its
+            // first half and the per-chunk moment partials in its second.
+            const int chunks = C / kGramN < 8 ? C / kGramN : 8;
+            if (chunks >= 1) {
+                float2* gnf = reinterpret_cast<float2*>(gn_sums);
+                double* part = gn_sums + (size_t)n_utt * C;
+                conv0_gram_kernel<<<dim3(chunks, n_utt), kGramThreads, 0, S(stream)>>>(audio, off, frames, chunks,
+                                                                                        part);
+                int rc = launch_rc();
+                if (rc) return rc;
+                conv0_gram_finalize_kernel<<<n_utt, 512, 0, S(stream)>>>(part, chunks, stats, frames, w0, b0, C,
+                                                                         gnf);
+                rc = launch_rc();
+                if (rc) return rc;
+                a.gnf = gnf;
+            } else {
+                if (cudaMemsetAsync(gn_sums, 0, sizeof(double) * 2 * C * (size_t)n_utt, S(stream)) != cudaSuccess)
+                    return W2V_ERR_LAUNCH;
+                const size_t sh = (size_t)((kC0StatFrames - 1) * s0 + k0 + kC0MaxK + kC0Win) * sizeof(float);
+                dim3 g((max_frames + kC0StatFrames - 1) / kC0StatFrames, n_utt);
+                conv0x4_gn_stats_kernel<<<g, 128, sh, S(stream)>>>(a);
+                int rc = launch_rc();
+                if (rc) return rc;
+            }
         }
         const size_t sh = (size_t)((kC0ApplyFrames - 1) * s0 + k0 + kC0MaxK + kC0Win) * sizeof(float);
         dim3 g((max_frames + kC0ApplyFrames - 1) / kC0ApplyFrames, n_utt);

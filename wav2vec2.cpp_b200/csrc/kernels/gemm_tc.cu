@@ -55,10 +55,11 @@ struct GemmParams {
 
 template <int BN>
 struct GemmCfg {
-    static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+    static constexpr int kStages = BN == 256 ? 4 : BN == 192 ? 4 : BN == 128 ? 6 : 8;
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
-    static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+    // two accumulators; TMEM is allocated in powers of two columns
+    static constexpr int kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
     static constexpr int kSmem = kStages * (kABytes + kBBytes) + kStageBytes + 1024 + 256;
 };
 
@@ -410,8 +411,8 @@ template <int BN>
 struct Gemm2Cfg {
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = (BN / 2) * kBK * 2;
-    static constexpr int kStages = BN == 256 ? 6 : 8;
-    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kStages = BN == 256 ? 6 : BN == 192 ? 6 : 8;
+    static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
     static constexpr int kSmem = kStages * (kABytes + kBBytes) + kStageBytes + 1024 + 256;
 };
 
@@ -671,8 +672,10 @@ template <int EPI>
 static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
     switch (bn) {
         case 256: return launch_bn<256, EPI>(ta, tb, p, st);
+        case 192: return launch_bn<192, EPI>(ta, tb, p, st);
         case 128: return launch_bn<128, EPI>(ta, tb, p, st);
         case -256: return launch_pair<256, EPI>(ta, tb, p, st);
+        case -192: return launch_pair<192, EPI>(ta, tb, p, st);
         case -128: return launch_pair<128, EPI>(ta, tb, p, st);
         default: return launch_bn<64, EPI>(ta, tb, p, st);
     }
@@ -687,7 +690,8 @@ static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb, cons
 //      GELU < fp32 residual), only partly hidden behind the next tile's MMAs;
 //   e  pairs wait for both CTAs' epilogues before reusing an accumulator.
 // Constants fitted on B200 to the encoder GEMMs (M = 31936, K = 768/3072,
-// N = 768/2304/3072, every epilogue), within about 5 % of measured times.
+// N = 768/2304/3072, every epilogue, every tile): the model picks the
+// measured-fastest tile for each of them.
 static int pick_bn(int N, int m_valid, int n_batch, long long K, int epilogue) {
     const int sms = sm_count();
     const long long mt1 = (long long)((m_valid + kBM - 1) / kBM) * n_batch;
@@ -696,13 +700,14 @@ static int pick_bn(int N, int m_valid, int n_batch, long long K, int epilogue) {
                    : epilogue == W2V_EPI_F32 ? 450 : 932;
     int best = 64;
     double best_cost = 1e300;
-    for (int bn : {256, 128, 64, -256, -128}) {
+    for (int bn : {256, 192, 128, 64, -256, -192, -128}) {
         const int w = bn < 0 ? -bn : bn;
         if (N % w != 0 && bn != 64) continue;
         const long long tiles = (bn < 0 ? mt2 : mt1) * ((N + w - 1) / w);
         const long long slots = bn < 0 ? sms / 2 : sms;
         const long long waves = (tiles + slots - 1) / slots;
-        const double m = bn == 256 ? 1.0 : bn == 128 ? 1.3 : bn == 64 ? 1.6 : bn == -256 ? 0.78 : 1.3;
+        const double m = bn == 256 ? 1.0 : bn == 192 ? 1.15 : bn == 128 ? 1.3 : bn == 64 ? 1.6
+                       : bn == -256 ? 0.78 : bn == -192 ? 1.0 : 1.3;
         const double e = bn < 0 ? 1.34 : 1.0;
         const double cost = (double)waves * w * ((double)K * m + E * e);
         if (cost < best_cost) { best_cost = cost; best = bn; }
@@ -753,7 +758,8 @@ extern "C" int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_st
     p.n_batch = (int)a_batches;
     p.N = N;
     const int bn = block_n ? block_n : pick_bn(N, m_valid, p.n_batch, K, epilogue);
-    if (bn != 256 && bn != 128 && bn != 64 && bn != -256 && bn != -128) return W2V_ERR_ARGS;
+    if (bn != 256 && bn != 192 && bn != 128 && bn != 64 && bn != -256 && bn != -192 && bn != -128)
+        return W2V_ERR_ARGS;
     const int tile_rows = bn < 0 ? 2 * kBM : kBM, tile_cols = bn < 0 ? -bn : bn;
     p.m_tiles = (int)((m_valid + tile_rows - 1) / tile_rows);
     p.n_tiles = (N + tile_cols - 1) / tile_cols;

@@ -311,6 +311,39 @@ def write_wav_f32(path: str | Path, x: np.ndarray, sr: int = 16000) -> None:
     Path(path).write_bytes(hdr + data)
 
 
+def wav_bytes(x: np.ndarray, sr: int = 16000, fmt: str = "pcm16", chunks_before: tuple = (),
+              fmt_size: int = 16, data_size: int | None = None, truncate: int = 0) -> bytes:
+    """RIFF/WAVE image of x ([n] or [n, channels], float in [-1, 1]).
+    fmt: "pcm16", "pcm32" (integer PCM, rounded and clipped) or "f32" (IEEE
+    float).  chunks_before: (4-byte id, payload) chunks placed between "fmt "
+    and "data"; fmt_size > 16 pads the fmt chunk (WAVE_FORMAT_EX style);
+    data_size overrides the declared data length; truncate drops bytes from
+    the end of the image."""
+    x = np.asarray(x, np.float64)
+    if x.ndim == 1:
+        x = x[:, None]
+    n, ch = x.shape
+    if fmt == "pcm16":
+        data = np.clip(np.round(x * 32768.0), -32768, 32767).astype("<i2").tobytes()
+        code, bits = 1, 16
+    elif fmt == "pcm32":
+        data = np.clip(np.round(x * 2147483648.0), -2147483648, 2147483647).astype("<i4").tobytes()
+        code, bits = 1, 32
+    elif fmt == "f32":
+        data = x.astype("<f4").tobytes()
+        code, bits = 3, 32
+    else:
+        raise ValueError(fmt)
+    blk = ch * bits // 8
+    fmt_body = struct.pack("<HHIIHH", code, ch, sr, sr * blk, blk, bits) + b"\0" * (fmt_size - 16)
+    body = b"WAVE" + b"fmt " + struct.pack("<I", fmt_size) + fmt_body
+    for cid, payload in chunks_before:
+        body += cid + struct.pack("<I", len(payload)) + payload
+    body += b"data" + struct.pack("<I", len(data) if data_size is None else data_size) + data
+    img = b"RIFF" + struct.pack("<I", len(body)) + body
+    return img[:len(img) - truncate] if truncate else img
+
+
 def n_frames(n_samples: int, arch: Arch | str = "base") -> int:
     """Conv extractor output length (reference wav2vec2.cpp:278)."""
     if isinstance(arch, str):
