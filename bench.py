@@ -312,10 +312,15 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
             "config": workload(args),
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel on the encoder linears (tcgen05, TMEM)",
+            "roofline": {"bound": "tensor",
+                         "kernel": "gemm_tc_kernel / gemm2_tc_kernel on the encoder linears (tcgen05, TMEM)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak if peak else None, "traffic": None,
+                         "frac": achieved / peak if peak else None,
+                         "traffic": encoder_gemm_traffic(args),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of each "
+                                           "encoder linear at this workload, mean per launch",
                          "peak_source": f"bf16 dense sustained, {pk_src}",
+                         "frac_of_burst_peak": achieved / pk["bf16_tflops"] if pk.get("bf16_tflops") else None,
                          "launches": g["launches"], "avg_launch_ms": g["ms"] / max(1, g["launches"]),
                          "flops_per_launch": g["flops"] / max(1, g["launches"])},
             "step_tflops": total_flops / steps_prof / (elapsed_ms / args.steps / 1000.0) / 1e12,
@@ -338,6 +343,20 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# DRAM bytes per launch of the four encoder linears of wav2vec2-base at 64 x
+# 499 rows (QKV, attention out-projection + residual, FFN up + GELU, FFN down +
+# residual), measured with ncu on B200 on one launch each.
+ENCODER_GEMM_DRAM_BYTES = {"qkv": 148.0e6, "out_proj": 188.4e6, "ffn_up": 198.5e6, "ffn_down": 372.5e6}
+
+
+def encoder_gemm_traffic(args):
+    """Mean DRAM traffic per encoder-GEMM launch for the default workload
+    (None for other workloads, which were not captured)."""
+    if (args.dtype, args.batch, args.seconds) != ("q8_0", 64, 10.0):
+        return None
+    return sum(ENCODER_GEMM_DRAM_BYTES.values()) / len(ENCODER_GEMM_DRAM_BYTES)
 
 
 def run_kernel_case(args):

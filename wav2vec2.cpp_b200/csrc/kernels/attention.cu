@@ -180,28 +180,36 @@ attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, const long
 // One CTA per (utterance, head, 128-query tile); 192 threads:
 //   warp 0      TMA: Q once, then K/V tiles of 128 keys through a 2-stage ring
 //   warp 1      one thread issues tcgen05.mma: S = Q K^T into TMEM, then
-//               O += P V with P (fp16, smem, K-major) and V straight from its
-//               TMA tile as an MN-major operand
-//   warps 2..5  softmax, one query row per thread (its TMEM lane): online
-//               max/sum in fp32, P written to smem in the 128-byte swizzle
-//               layout, O rescaled in TMEM when the running max moves.
-// Handoffs use mbarriers with bounded waits.  TMEM: S at columns 0..127, O at
-// 128..128+D.
+//               O += P V with P read from TMEM (A operand) and V straight from
+//               its TMA tile as an MN-major shared-memory operand
+//   warps 2..5  softmax, one query row per thread (its TMEM lane), in two
+//               passes over S (row max, then 2^x and P) so only 32 scores
+//               are live in registers; P is packed to fp16 into its own TMEM
+//               columns.
+// The running max used as the exponent reference is only raised when the
+// row max exceeds it by more than 2^8 (in the exp2 domain): P then stays
+// <= 256 (exact in fp16 range) and the O rescale in TMEM is rare.  The sum
+// and O use the same reference, so the result is unchanged.
+// Ordering: every S(j) commit also covers PV(j-1), so once the softmax sees
+// S(j) it may rescale O and overwrite P; the MMA issues PV(j) only after the
+// softmax has published P(j).  Handoffs use mbarriers with bounded waits.
+// TMEM: S at columns 0..127, P at 128..191, O at 192.. (D = 64: 256 columns,
+// two CTAs per SM; D = 128: 512 columns).
 template <int D>
 struct AttnTc {
     static constexpr int kAtoms = D / 64;               // 64-column swizzle atoms per row
     static constexpr int kTile = 128 * D * 2;           // one Q, K or V tile
     static constexpr int kAtomBytes = 128 * 64 * 2;     // 16 KB
-    static constexpr int kPBytes = 128 * 128 * 2;       // P: 2 atoms of 64 keys
-    // D = 64: one K/V stage keeps the CTA at ~81 KB so two CTAs share an SM and
-    // hide each other's loads; D = 128: two stages, one CTA per SM.
-    static constexpr int kStages = D == 64 ? 1 : 2;
-    static constexpr int kSmem = kTile + kStages * 2 * kTile + kPBytes + 1024 + 128;
-    static constexpr int kTmemCols = 256;
+    static constexpr int kStages = 2;
+    static constexpr int kSmem = kTile + kStages * 2 * kTile + 1024 + 128;
+    static constexpr int kColP = 128, kColO = 192;
+    static constexpr int kTmemCols = kColO + D <= 256 ? 256 : 512;
 };
 
+constexpr float kLazyRescaleLog2 = 8.f;
+
 template <int D>
-__global__ void __launch_bounds__(192)
+__global__ void __launch_bounds__(192, 2)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out, const long long* __restrict__ off,
                const int* __restrict__ Tn, int H, float scale_log2, int* err) {
     using Cfg = AttnTc<D>;
@@ -217,25 +225,22 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     uint8_t* sQ = smem;
     uint8_t* sKV = sQ + Cfg::kTile;
-    uint8_t* sP = sKV + Cfg::kStages * 2 * Cfg::kTile;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sP + Cfg::kPBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + Cfg::kStages * 2 * Cfg::kTile);
     uint64_t* q_full = bars;
     uint64_t* kv_full = bars + 1;                     // [kStages]
     uint64_t* kv_empty = bars + 1 + Cfg::kStages;     // [kStages]
     uint64_t* s_full = bars + 1 + 2 * Cfg::kStages;
-    uint64_t* s_free = s_full + 1;
-    uint64_t* p_full = s_full + 2;
-    uint64_t* o_done = s_full + 3;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 4);
+    uint64_t* p_full = s_full + 1;
+    uint64_t* o_full = s_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 3);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int s = 0; s < Cfg::kStages; s++) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
         mbar_init(s_full, 1);
-        mbar_init(s_free, 4);
         mbar_init(p_full, 4);
-        mbar_init(o_done, 1);
+        mbar_init(o_full, 1);
         fence_mbar_init();
         tma_prefetch_desc(&tm);
     }
@@ -244,7 +249,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t tS = tmem_base, tO = tmem_base + 128;
+    const uint32_t tS = tmem_base, tP = tmem_base + Cfg::kColP, tO = tmem_base + Cfg::kColO;
     const int colQ = h * D, colK = H + h * D, colV = 2 * H + h * D;
 
     if (warp == 0) {
@@ -269,6 +274,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
                 last_par = (last_par & ~(1u << stage)) | (phase << stage);
                 if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
             }
+            // never leave with a bulk copy still writing shared memory
             mbar_wait(q_full, 0, err);
             for (int s = 0; s < Cfg::kStages; s++)
                 if (issued & (1u << s)) mbar_wait(&kv_full[s], (last_par >> s) & 1u, err);
@@ -283,7 +289,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
             bool ok = mbar_wait(q_full, 0, err);
             for (int j = 0; j < n_kv && ok; j++) {
                 if (!mbar_wait(&kv_full[stage], phase, err)) break;
-                if (j > 0 && !mbar_wait(s_free, (uint32_t)(j - 1) & 1u, err)) break;
                 tc_fence_after();
                 const uint32_t q_addr = smem_u32(sQ);
                 const uint32_t k_addr = smem_u32(sKV + stage * 2 * Cfg::kTile);
@@ -296,92 +301,81 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
                 umma_commit(s_full);
                 if (!mbar_wait(p_full, (uint32_t)j & 1u, err)) break;
                 tc_fence_after();
-                const uint32_t p_addr = smem_u32(sP);
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t po = (kk / 4) * Cfg::kAtomBytes + (kk % 4) * 32;
-                    umma_f16(tO, umma_desc_sw128(p_addr + po), umma_desc_sw128_mn(v_addr + kk * 2048, Cfg::kAtomBytes),
-                             idesc_o, (j > 0 || kk > 0));
-                }
+                for (int kk = 0; kk < 8; kk++)
+                    umma_f16_tmem_a(tO, tP + (uint32_t)(kk * 8), umma_desc_sw128_mn(v_addr + kk * 2048, Cfg::kAtomBytes),
+                                    idesc_o, (j > 0 || kk > 0));
                 umma_commit(&kv_empty[stage]);
-                umma_commit(o_done);
                 if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
             }
+            umma_commit(o_full);   // also reached on error: completes once the issued MMAs have
         }
         __syncwarp();
     } else {
         const int qd = warp & 3;                       // TMEM lane quarter
         const int row = qd * 32 + lane;
         const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
-        float m = -INFINITY, l = 0.f;
+        float m = -INFINITY, l = 0.f;                  // exponent reference (raw score units) and row sum
         bool ok = true;
         for (int j = 0; j < n_kv && ok; j++) {
             if (!mbar_wait(s_full, (uint32_t)j & 1u, err)) { ok = false; break; }
             tc_fence_after();
-            float sv[128];
+            const int kb = j * 128;
+            const int nvalid = T - kb < 128 ? T - kb : 128;   // keys of this tile inside the utterance
+            // pass 1: row max
+            float mx = -INFINITY;
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 float t[32];
                 tmem_ld32(tS + lane_off + c * 32, t);
 #pragma unroll
-                for (int i = 0; i < 32; i++) sv[c * 32 + i] = t[i];
+                for (int i = 0; i < 32; i++)
+                    if (c * 32 + i < nvalid) mx = fmaxf(mx, t[i]);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_free);
-            const int kb = j * 128;
-            if (kb + 128 > T) {
-#pragma unroll
-                for (int c = 0; c < 128; c++)
-                    if (kb + c >= T) sv[c] = -INFINITY;
+            const bool raise = (mx - m) * scale_log2 > kLazyRescaleLog2;   // always at j == 0
+            float o_scale = 1.f;
+            if (raise) {
+                o_scale = ex2_sfu((m - mx) * scale_log2);      // 0 at j == 0
+                l *= o_scale;
+                m = mx;
             }
-            float mx = m;
-#pragma unroll
-            for (int c = 0; c < 128; c++) mx = fmaxf(mx, sv[c]);
-            const float alpha = exp2f((m - mx) * scale_log2);
-            const float mxs = mx * scale_log2;
-            float sum = 0.f;
-#pragma unroll
-            for (int c = 0; c < 128; c++) {
-                sv[c] = exp2f(fmaf(sv[c], scale_log2, -mxs));
-                sum += sv[c];
-            }
-            l = l * alpha + sum;
-            m = mx;
-            if (j > 0) {
-                if (!mbar_wait(o_done, (uint32_t)(j - 1) & 1u, err)) { ok = false; break; }
-                tc_fence_after();
-            }
-            // P row -> smem (fp16, K-major, 128-byte swizzle: chunk c8 of row r at (c8 ^ (r & 7)))
-#pragma unroll
-            for (int ch = 0; ch < 16; ch++) {
-                uint4 pk;
-                pk.x = pack_half2(sv[ch * 8 + 0], sv[ch * 8 + 1]);
-                pk.y = pack_half2(sv[ch * 8 + 2], sv[ch * 8 + 3]);
-                pk.z = pack_half2(sv[ch * 8 + 4], sv[ch * 8 + 5]);
-                pk.w = pack_half2(sv[ch * 8 + 6], sv[ch * 8 + 7]);
-                uint8_t* dst = sP + (ch / 8) * Cfg::kAtomBytes + row * 128 + (((ch % 8) ^ (row & 7)) * 16);
-                *reinterpret_cast<uint4*>(dst) = pk;
-            }
-            // rescale the running output when any row's max moved
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+            // O holds PV(0..j-1), complete (the S(j) commit covered it)
+            if (j > 0 && __any_sync(0xffffffffu, raise)) {
 #pragma unroll
                 for (int a = 0; a < D / 32; a++) {
                     float t[32];
                     tmem_ld32(tO + lane_off + a * 32, t);
 #pragma unroll
-                    for (int i = 0; i < 32; i++) t[i] *= alpha;
+                    for (int i = 0; i < 32; i++) t[i] *= o_scale;
                     tmem_st32(tO + lane_off + a * 32, t);
                 }
             }
-            fence_async_smem();
+            // pass 2: P = 2^(s*scale - m*scale) in fp16, into TMEM columns of P
+            const float ms = m * scale_log2;
+            float sum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float t[32];
+                tmem_ld32(tS + lane_off + c * 32, t);
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const float p0 = c * 32 + i < nvalid ? ex2_sfu(fmaf(t[i], scale_log2, -ms)) : 0.f;
+                    const float p1 = c * 32 + i + 1 < nvalid ? ex2_sfu(fmaf(t[i + 1], scale_log2, -ms)) : 0.f;
+                    sum += p0 + p1;
+                    pk[i / 2] = pack_half2(p0, p1);
+                }
+                tmem_st16(tP + lane_off + c * 16, pk);
+            }
+            l += sum;
+            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
         }
-        if (ok && mbar_wait(o_done, (uint32_t)(n_kv - 1) & 1u, err)) {
+        if (ok && mbar_wait(o_full, 0, err)) {
             tc_fence_after();
-            const float inv = 1.f / l;
+            const float inv = __fdividef(1.f, l);
             const bool valid = q0 + row < T;
             __half* o = out + (base + q0 + row) * (long long)H + (long long)h * D;
 #pragma unroll
