@@ -178,54 +178,63 @@ attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, const long
 
 // ── tcgen05 flash attention (head dim 64 or 128) ────────────────────────────
 // One CTA per (utterance, head, 128-query tile); 192 threads:
-//   warp 0      TMA: Q once, then K/V tiles of 128 keys through a 2-stage ring
+//   warp 0      TMA: Q once, then K/V tiles of KV keys through a 2-stage ring
 //   warp 1      one thread issues tcgen05.mma: S = Q K^T into TMEM, then
 //               O += P V with P read from TMEM (A operand) and V straight from
 //               its TMA tile as an MN-major shared-memory operand
 //   warps 2..5  softmax, one query row per thread (its TMEM lane), in two
 //               passes over S (row max, then 2^x and P) so only 32 scores
-//               are live in registers; P is packed to fp16 into its own TMEM
-//               columns.
+//               are live in registers; P is packed to fp16 over the first
+//               KV/2 columns of S (each 32-score chunk is read before the 16
+//               columns it overwrites).
 // The running max used as the exponent reference is only raised when the
 // row max exceeds it by more than 2^8 (in the exp2 domain): P then stays
 // <= 256 (exact in fp16 range) and the O rescale in TMEM is rare.  The sum
 // and O use the same reference, so the result is unchanged.
-// Ordering: every S(j) commit also covers PV(j-1), so once the softmax sees
-// S(j) it may rescale O and overwrite P; the MMA issues PV(j) only after the
-// softmax has published P(j).  Handoffs use mbarriers with bounded waits.
-// TMEM: S at columns 0..127, P at 128..191, O at 192.. (D = 64: 256 columns,
-// two CTAs per SM; D = 128: 512 columns).
-template <int D>
+// Ordering: one thread issues every MMA, in order: PV(j) (which reads P(j)
+// from S's columns) before S(j+1) (which overwrites them).  Every S(j)
+// commit also covers PV(j-1), so once the softmax sees S(j) it may rescale
+// O and write P; the MMA issues PV(j) only after the softmax has published
+// P(j).  Handoffs use mbarriers with bounded waits.
+// TMEM: S/P at columns 0..KV-1, O at KV..KV+D-1.  With KV = 64 and D = 64 a
+// CTA holds 128 columns and 50 KB of shared memory, so four CTAs share an SM
+// and hide each other's handoff latencies.
+template <int D, int KV>
 struct AttnTc {
     static constexpr int kAtoms = D / 64;               // 64-column swizzle atoms per row
-    static constexpr int kTile = 128 * D * 2;           // one Q, K or V tile
-    static constexpr int kAtomBytes = 128 * 64 * 2;     // 16 KB
+    static constexpr int kTileQ = 128 * D * 2;
+    static constexpr int kTileKV = KV * D * 2;          // one K or V tile
+    static constexpr int kAtomQ = 128 * 128;            // 128 rows x 128 B
+    static constexpr int kAtomKV = KV * 128;
     static constexpr int kStages = 2;
-    static constexpr int kSmem = kTile + kStages * 2 * kTile + 1024 + 128;
-    static constexpr int kColP = 128, kColO = 192;
-    static constexpr int kTmemCols = kColO + D <= 256 ? 256 : 512;
+    static constexpr int kSmem = kTileQ + kStages * 2 * kTileKV + 1024 + 128;
+    static constexpr int kColO = KV;
+    static constexpr int kTmemCols = KV + D <= 128 ? 128 : KV + D <= 256 ? 256 : 512;
+    static constexpr int kMinBlocks = kTmemCols <= 128 ? 4 : 2;
 };
 
 constexpr float kLazyRescaleLog2 = 8.f;
 
-template <int D>
-__global__ void __launch_bounds__(192, 2)
-attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out, const long long* __restrict__ off,
-               const int* __restrict__ Tn, int H, float scale_log2, int* err) {
-    using Cfg = AttnTc<D>;
+template <int D, int KV>
+__global__ void __launch_bounds__(192, AttnTc<D, KV>::kMinBlocks)
+attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
+               __half* __restrict__ out, const long long* __restrict__ off, const int* __restrict__ Tn, int H,
+               float scale_log2, int* err) {
+    using Cfg = AttnTc<D, KV>;
+    constexpr int kChunks = KV / 32;
     const int u = blockIdx.z, h = blockIdx.y;
     const int T = Tn[u];
     const int q0 = blockIdx.x * 128;
     if (q0 >= T) return;
     const long long base = off[u];
-    const int n_kv = (T + 127) / 128;
+    const int n_kv = (T + KV - 1) / KV;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     uint8_t* sQ = smem;
-    uint8_t* sKV = sQ + Cfg::kTile;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + Cfg::kStages * 2 * Cfg::kTile);
+    uint8_t* sKV = sQ + Cfg::kTileQ;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + Cfg::kStages * 2 * Cfg::kTileKV);
     uint64_t* q_full = bars;
     uint64_t* kv_full = bars + 1;                     // [kStages]
     uint64_t* kv_empty = bars + 1 + Cfg::kStages;     // [kStages]
@@ -242,33 +251,34 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
         mbar_init(p_full, 4);
         mbar_init(o_full, 1);
         fence_mbar_init();
-        tma_prefetch_desc(&tm);
+        tma_prefetch_desc(&tmq);
+        tma_prefetch_desc(&tmkv);
     }
     if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t tS = tmem_base, tP = tmem_base + Cfg::kColP, tO = tmem_base + Cfg::kColO;
+    const uint32_t tS = tmem_base, tO = tmem_base + Cfg::kColO;
     const int colQ = h * D, colK = H + h * D, colV = 2 * H + h * D;
 
     if (warp == 0) {
         if (elect_one()) {
-            mbar_arrive_expect_tx(q_full, Cfg::kTile);
+            mbar_arrive_expect_tx(q_full, Cfg::kTileQ);
 #pragma unroll
             for (int a = 0; a < Cfg::kAtoms; a++)
-                tma_load_2d(sQ + a * Cfg::kAtomBytes, &tm, q_full, colQ + 64 * a, (int)(base + q0));
+                tma_load_2d(sQ + a * Cfg::kAtomQ, &tmq, q_full, colQ + 64 * a, (int)(base + q0));
             int stage = 0;
             uint32_t phase = 0, issued = 0, last_par = 0;
             for (int j = 0; j < n_kv; j++) {
                 if (!mbar_wait(&kv_empty[stage], phase ^ 1u, err)) break;
-                mbar_arrive_expect_tx(&kv_full[stage], 2 * Cfg::kTile);
-                uint8_t* sK = sKV + stage * 2 * Cfg::kTile;
-                uint8_t* sV = sK + Cfg::kTile;
+                mbar_arrive_expect_tx(&kv_full[stage], 2 * Cfg::kTileKV);
+                uint8_t* sK = sKV + stage * 2 * Cfg::kTileKV;
+                uint8_t* sV = sK + Cfg::kTileKV;
 #pragma unroll
                 for (int a = 0; a < Cfg::kAtoms; a++) {
-                    tma_load_2d(sK + a * Cfg::kAtomBytes, &tm, &kv_full[stage], colK + 64 * a, (int)(base + j * 128));
-                    tma_load_2d(sV + a * Cfg::kAtomBytes, &tm, &kv_full[stage], colV + 64 * a, (int)(base + j * 128));
+                    tma_load_2d(sK + a * Cfg::kAtomKV, &tmkv, &kv_full[stage], colK + 64 * a, (int)(base + j * KV));
+                    tma_load_2d(sV + a * Cfg::kAtomKV, &tmkv, &kv_full[stage], colV + 64 * a, (int)(base + j * KV));
                 }
                 issued |= 1u << stage;
                 last_par = (last_par & ~(1u << stage)) | (phase << stage);
@@ -282,7 +292,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
         __syncwarp();
     } else if (warp == 1) {
         if (elect_one()) {
-            constexpr uint32_t idesc_s = umma_idesc_f16(128, 128);
+            constexpr uint32_t idesc_s = umma_idesc_f16(128, KV);
             constexpr uint32_t idesc_o = umma_idesc_f16_bmn(128, D);
             int stage = 0;
             uint32_t phase = 0;
@@ -291,19 +301,20 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
                 if (!mbar_wait(&kv_full[stage], phase, err)) break;
                 tc_fence_after();
                 const uint32_t q_addr = smem_u32(sQ);
-                const uint32_t k_addr = smem_u32(sKV + stage * 2 * Cfg::kTile);
-                const uint32_t v_addr = k_addr + Cfg::kTile;
+                const uint32_t k_addr = smem_u32(sKV + stage * 2 * Cfg::kTileKV);
+                const uint32_t v_addr = k_addr + Cfg::kTileKV;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++) {
-                    const uint32_t o = (kk / 4) * Cfg::kAtomBytes + (kk % 4) * 32;
-                    umma_f16(tS, umma_desc_sw128(q_addr + o), umma_desc_sw128(k_addr + o), idesc_s, kk > 0);
+                    const uint32_t oq = (kk / 4) * Cfg::kAtomQ + (kk % 4) * 32;
+                    const uint32_t ok_ = (kk / 4) * Cfg::kAtomKV + (kk % 4) * 32;
+                    umma_f16(tS, umma_desc_sw128(q_addr + oq), umma_desc_sw128(k_addr + ok_), idesc_s, kk > 0);
                 }
                 umma_commit(s_full);
                 if (!mbar_wait(p_full, (uint32_t)j & 1u, err)) break;
                 tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++)
-                    umma_f16_tmem_a(tO, tP + (uint32_t)(kk * 8), umma_desc_sw128_mn(v_addr + kk * 2048, Cfg::kAtomBytes),
+                for (int kk = 0; kk < KV / 16; kk++)
+                    umma_f16_tmem_a(tO, tS + (uint32_t)(kk * 8), umma_desc_sw128_mn(v_addr + kk * 2048, Cfg::kAtomKV),
                                     idesc_o, (j > 0 || kk > 0));
                 umma_commit(&kv_empty[stage]);
                 if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
@@ -320,17 +331,22 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
         for (int j = 0; j < n_kv && ok; j++) {
             if (!mbar_wait(s_full, (uint32_t)j & 1u, err)) { ok = false; break; }
             tc_fence_after();
-            const int kb = j * 128;
-            const int nvalid = T - kb < 128 ? T - kb : 128;   // keys of this tile inside the utterance
+            const int nvalid = T - j * KV < KV ? T - j * KV : KV;   // keys of this tile inside the utterance
+            const bool full = nvalid == KV;
             // pass 1: row max
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
+            for (int c = 0; c < kChunks; c++) {
                 float t[32];
                 tmem_ld32(tS + lane_off + c * 32, t);
+                if (full) {
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    if (c * 32 + i < nvalid) mx = fmaxf(mx, t[i]);
+                    for (int i = 0; i < 32; i++) mx = fmaxf(mx, t[i]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i++)
+                        if (c * 32 + i < nvalid) mx = fmaxf(mx, t[i]);
+                }
             }
             const bool raise = (mx - m) * scale_log2 > kLazyRescaleLog2;   // always at j == 0
             float o_scale = 1.f;
@@ -350,24 +366,36 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __half* __restrict__ out,
                     tmem_st32(tO + lane_off + a * 32, t);
                 }
             }
-            // pass 2: P = 2^(s*scale - m*scale) in fp16, into TMEM columns of P
+            // pass 2: P = 2^(s*scale - m*scale) in fp16 over S's first KV/2 columns
             const float ms = m * scale_log2;
-            float sum = 0.f;
+            float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
+            for (int c = 0; c < kChunks; c++) {
                 float t[32];
                 tmem_ld32(tS + lane_off + c * 32, t);
                 uint32_t pk[16];
+                if (full) {
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float p0 = c * 32 + i < nvalid ? ex2_sfu(fmaf(t[i], scale_log2, -ms)) : 0.f;
-                    const float p1 = c * 32 + i + 1 < nvalid ? ex2_sfu(fmaf(t[i + 1], scale_log2, -ms)) : 0.f;
-                    sum += p0 + p1;
-                    pk[i / 2] = pack_half2(p0, p1);
+                    for (int i = 0; i < 32; i += 2) {
+                        const float p0 = ex2_sfu(fmaf(t[i], scale_log2, -ms));
+                        const float p1 = ex2_sfu(fmaf(t[i + 1], scale_log2, -ms));
+                        sum0 += p0;
+                        sum1 += p1;
+                        pk[i / 2] = pack_half2(p0, p1);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        const float p0 = c * 32 + i < nvalid ? ex2_sfu(fmaf(t[i], scale_log2, -ms)) : 0.f;
+                        const float p1 = c * 32 + i + 1 < nvalid ? ex2_sfu(fmaf(t[i + 1], scale_log2, -ms)) : 0.f;
+                        sum0 += p0;
+                        sum1 += p1;
+                        pk[i / 2] = pack_half2(p0, p1);
+                    }
                 }
-                tmem_st16(tP + lane_off + c * 16, pk);
+                tmem_st16(tS + lane_off + c * 16, pk);
             }
-            l += sum;
+            l += sum0 + sum1;
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -416,18 +444,22 @@ static PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
     return fn;
 }
 
-template <int D>
+template <int D, int KV>
 static int launch_attn_tc(const void* qkv, void* out, const long long* off, const int* T, int n_utt, int H,
                           int n_heads, int max_T, long long M, int* err, cudaStream_t st) {
-    using Cfg = AttnTc<D>;
+    using Cfg = AttnTc<D, KV>;
     auto enc = attn_encode_fn();
     if (!enc) return W2V_ERR_DRIVER;
-    CUtensorMap tm;
+    // two views of qkv [M][3H]: 128-row boxes for Q, KV-row boxes for K and V
+    CUtensorMap tmq, tmkv;
     const uint64_t dims[2] = {(uint64_t)3 * H, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)3 * H * 2};
-    const uint32_t box[2] = {64, 128};
     const uint32_t es[2] = {1, 1};
-    if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(qkv), dims, strides, box, es,
+    const uint32_t boxq[2] = {64, 128}, boxkv[2] = {64, (uint32_t)KV};
+    if (enc(&tmq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(qkv), dims, strides, boxq, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&tmkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(qkv), dims, strides, boxkv, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return W2V_ERR_TENSOR_MAP;
@@ -435,14 +467,14 @@ static int launch_attn_tc(const void* qkv, void* out, const long long* off, cons
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {
-        if (cudaFuncSetAttribute(attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
+        if (cudaFuncSetAttribute(attn_tc_kernel<D, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
             cudaSuccess)
             return W2V_ERR_LAUNCH;
         attr[dev & 63] = true;
     }
     const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     dim3 grid((max_T + 127) / 128, n_heads, n_utt);
-    attn_tc_kernel<D><<<grid, 192, Cfg::kSmem, st>>>(tm, (__half*)out, off, T, H, scale_log2, err);
+    attn_tc_kernel<D, KV><<<grid, 192, Cfg::kSmem, st>>>(tmq, tmkv, (__half*)out, off, T, H, scale_log2, err);
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
@@ -476,11 +508,11 @@ extern "C" int w2v_attention(const void* qkv, void* out, const long long* off, c
     const bool tma_ok = (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && H % 64 == 0;
     switch (d) {
         case 64:
-            if (tma_ok) return w2v::launch_attn_tc<64>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+            if (tma_ok) return w2v::launch_attn_tc<64, 64>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
             return w2v::launch_attn<64>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         case 80: return w2v::launch_attn<80>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         case 128:
-            if (tma_ok) return w2v::launch_attn_tc<128>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+            if (tma_ok) return w2v::launch_attn_tc<128, 64>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
             return w2v::launch_attn<128>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         default: return W2V_ERR_ARGS;
     }

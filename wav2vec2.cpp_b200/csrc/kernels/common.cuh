@@ -418,3 +418,4 @@ W2V_DEV float ex2_sfu(float x) {
     return y;
 }
 }  // namespace w2v
+
