@@ -115,12 +115,15 @@ int w2v_layer_norm(const void* in, int in_f16, long long ld_in, long long in_bat
 
 /* Positional conv embedding (src/wav2vec2.cpp:349-356): grouped conv1d over
  * time (kernel Kp, padding Kp/2, G groups, first T of T+1 outputs), GELU,
- * added to x in place.  x: fp32 packed rows [M, H]; utterance u occupies rows
+ * added to the input.  x: fp32 packed rows [M, H]; utterance u occupies rows
  * off[u] .. off[u]+T[u]; x = xin + gelu(conv(xin) + bias), x != xin.
- * wt: fp16 weights re-laid out by the engine as [G][Kp][H/G (co)][H/G (ci)];
- * bias fp32 [H].  H/G must be 32, 48, 64 or 80. */
+ * wt: fp16 weights re-laid out by the engine as
+ * [G][Kp][Cg/8][Cg (co)][8 (ci within the chunk)], Cg = H/G (one contiguous
+ * block of 8-row x 16-byte core matrices per tap); bias fp32 [H].
+ * Cg must be 32, 48, 64 or 80; Kp a multiple of 4, at most 128; x, xin, wt
+ * and bias 16-byte aligned.  err: device word for bounded-wait failures. */
 int w2v_pos_conv(float* x, const float* xin, const long long* off, const int* T, int n_utt, int H,
-                 int Kp, int G, const void* wt, const float* bias, int max_T, void* stream);
+                 int Kp, int G, const void* wt, const float* bias, int max_T, int* err, void* stream);
 
 /* Bidirectional multi-head attention (src/wav2vec2.cpp:293-334), flash-style
  * online softmax in fp32, fp16 tensor-core products.  qkv: fp16 [M, 3H]

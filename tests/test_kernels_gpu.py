@@ -277,20 +277,24 @@ def test_layer_norm(K, D, f16in, gelu):
 def test_pos_conv(K, H, G, Kp):
     """Grouped positional conv + GELU + residual (src/wav2vec2.cpp:349-356)."""
     rng = np.random.default_rng(H)
-    T = [130, 7, 300]
+    T = [130, 7, 700, 512]
     off = np.concatenate([[0], np.cumsum(T)[:-1]]).astype(np.int64)
     M = sum(T)
     xin = rng.standard_normal((M, H)).astype(np.float16).astype(np.float32)
     Cg = H // G
     w = (rng.standard_normal((H, Cg, Kp)) * 0.02).astype(np.float16).astype(np.float32)
     b = (rng.standard_normal(H) * 0.1).astype(np.float32)
-    wt = w.reshape(G, Cg, Cg, Kp).transpose(0, 3, 1, 2).astype(np.float16).copy()   # [G][Kp][co][ci]
-    d_x = torch.zeros(M, H, device="cuda")
+    # [G][Kp][Cg/8 (ci chunk)][co][8 (ci)]
+    wt = (w.reshape(G, Cg, Cg // 8, 8, Kp).transpose(0, 4, 2, 1, 3).astype(np.float16).copy())
+    d_x = torch.full((M, H), float("nan"), device="cuda")
     d_xin, d_off, d_T, d_wt, d_b = dev(xin), dev(off), dev(np.array(T, np.int32)), dev(wt), dev(b)
+    err = err_word()
     K.pos_conv(d_x.data_ptr(), d_xin.data_ptr(), d_off.data_ptr(), d_T.data_ptr(), len(T), H, Kp, G,
-               d_wt.data_ptr(), d_b.data_ptr(), max(T), stream())
+               d_wt.data_ptr(), d_b.data_ptr(), max(T), err.data_ptr(), stream())
     torch.cuda.synchronize()
+    assert int(err.item()) == 0
     got = d_x.cpu().numpy()
+    assert np.isfinite(got).all()
     for u, t in enumerate(T):
         xs = torch.from_numpy(xin[off[u]:off[u] + t]).double()
         conv = torch.nn.functional.conv1d(xs.T[None], torch.from_numpy(w).double(), torch.from_numpy(b).double(),

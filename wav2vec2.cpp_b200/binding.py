@@ -67,7 +67,7 @@ SIGNATURES = {
     "w2v_conv0_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _ll, _i,
                                _vp]),
     "w2v_layer_norm": (_i, [_vp, _i, _ll, _ll, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _ll, _vp]),
-    "w2v_pos_conv": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp]),
+    "w2v_pos_conv": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp, _vp]),
     "w2v_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _ll, _vp, _vp]),
     "w2v_ctc_greedy": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _i, _vp]),
 }
@@ -278,9 +278,9 @@ class kernels:
                                            stream or None), "w2v_layer_norm")
 
     @staticmethod
-    def pos_conv(x, xin, off, T, n_utt, H, Kp, G, wt, bias, max_T, stream=0):
-        kernels.check(lib().w2v_pos_conv(x, xin, off, T, n_utt, H, Kp, G, wt, bias, max_T, stream or None),
-                      "w2v_pos_conv")
+    def pos_conv(x, xin, off, T, n_utt, H, Kp, G, wt, bias, max_T, err=0, stream=0):
+        kernels.check(lib().w2v_pos_conv(x, xin, off, T, n_utt, H, Kp, G, wt, bias, max_T, err or None,
+                                         stream or None), "w2v_pos_conv")
 
     @staticmethod
     def attention(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err=0, stream=0):

@@ -131,7 +131,7 @@ ModelConfig ModelConfig::from_gguf(const GgufFile& gf) {
     need(c.pos_g > 0 && c.hidden % c.pos_g == 0, "hidden not divisible by pos_conv_groups");
     const int cg = c.pos_g ? c.hidden / c.pos_g : 0;
     need(cg == 32 || cg == 48 || cg == 64 || cg == 80, "hidden/pos_conv_groups must be 32, 48, 64 or 80");
-    need(c.pos_k > 0 && c.pos_k % 2 == 0, "pos_conv_kernel must be even");
+    need(c.pos_k > 0 && c.pos_k % 4 == 0 && c.pos_k <= 128, "pos_conv_kernel must be a multiple of 4, at most 128");
     need(c.conv_k[0] <= 16, "first conv kernel must be <= 16");
     for (int i = 1; i < c.n_conv; i++)
         need(!(c.conv_norm[i] && c.group_norm), "GroupNorm is supported on conv layer 0 only");
@@ -272,7 +272,8 @@ void Engine::load(const GgufFile& gf) {
     proj_w_.ensure((size_t)H * C * 2);
     upload_linear(gf, "feature_projection.projection", H, C, proj_w_);
     upload_floats(proj_b_, floats_sized(gf, "feature_projection.projection.bias", H), stream_);
-    // positional conv [H][Cg][Kp] -> [G][Kp][co][ci] (src/wav2vec2.cpp:211-212)
+    // positional conv [H][Cg][Kp] (src/wav2vec2.cpp:211-212) -> per tap, 8-channel
+    // core-matrix blocks: [G][Kp][Cg/8 (ci chunk)][Cg (co)][8 (ci)]
     {
         const int G = c.pos_g, Cg = H / G, Kp = c.pos_k;
         auto w = floats_sized(gf, "encoder.pos_conv_embed.conv.weight", (size_t)H * Cg * Kp);
@@ -281,7 +282,8 @@ void Engine::load(const GgufFile& gf) {
             for (int oc = 0; oc < Cg; oc++)
                 for (int ic = 0; ic < Cg; ic++)
                     for (int k = 0; k < Kp; k++)
-                        r[(((size_t)g * Kp + k) * Cg + oc) * Cg + ic] = w[((size_t)(g * Cg + oc) * Cg + ic) * Kp + k];
+                        r[((((size_t)g * Kp + k) * (Cg / 8) + ic / 8) * Cg + oc) * 8 + ic % 8] =
+                            w[((size_t)(g * Cg + oc) * Cg + ic) * Kp + k];
         upload_f16(pos_w_, r, stream_);
         upload_floats(pos_b_, floats_sized(gf, "encoder.pos_conv_embed.conv.bias", H), stream_);
     }
@@ -519,7 +521,7 @@ void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, 
     float* x = x_.as<float>();
     launch(P_POSCONV, 2.0 * M * c.pos_k * (H / c.pos_g) * H, st, "pos_conv", [&] {
         return w2v_pos_conv(x, pbuf_.as<float>(), d_T_off_, d_T_, B, H, c.pos_k, c.pos_g, pos_w_.p,
-                            pos_b_.as<float>(), g.T_max, st);
+                            pos_b_.as<float>(), g.T_max, err_.as<int>(), st);
     });
     const int n_heads = c.n_heads;
     double attn_flops = 0;

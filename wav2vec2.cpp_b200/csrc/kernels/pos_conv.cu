@@ -2,141 +2,224 @@
 // padding Kp/2, G groups, first T of the T+1 outputs), GELU, residual add
 // (src/wav2vec2.cpp:349-356; conv src/ops.h:76-99).
 //
-// Implicit GEMM per (utterance, group, 128-frame tile): for every tap the A
-// operand is the fp16 input window shifted by one row, read straight out of a
-// shared-memory copy of the 128+Kp input rows with per-lane ldmatrix row
-// addresses (no im2col); the B operand is that tap's [co][ci] weight slice,
-// streamed through a double-buffered shared-memory ring.  fp16 operands,
-// fp32 accumulation.
+// tcgen05 implicit GEMM.  One CTA per (utterance, group, 512 output frames):
+// four 128-frame tiles, each a TMEM accumulator of Cg fp32 columns
+// (M = 128, N = Cg, K = Kp x Cg).  The CTA's fp16 input window (512 + Kp
+// frames x Cg channels, zero outside the utterance) is staged once in shared
+// memory in the K-major no-swizzle layout with a 16-byte row pitch:
+//   [Cg/8 channel chunks][window rows][8 channels]
+// Core matrices (8 rows x 16 B) are then contiguous at ANY row offset, so
+// the A operand of tap k for tile r is the same window addressed k rows
+// further on: no im2col and no reload per tap.  The weights, laid out at load
+// time as [G][Kp][Cg/8][Cg (co)][8 (ci)] fp16 (one contiguous core-matrix
+// block per tap), stream through a shared-memory ring, 4 taps per bulk copy.
+// Roles (192 threads): warp 0 bulk-copies weights; warp 1 issues the MMAs;
+// warps 2..5 stage the input window, then drain the accumulators:
+// out = xin + gelu(acc + bias).  fp16 operands, fp32 accumulation.  Every
+// mbarrier wait is bounded.
 #include "common.cuh"
 #include "w2v_kernels.h"
 
 namespace w2v {
 
-constexpr int kPcRows = 128;   // output frames per block (8 warps x 16)
+constexpr int kPcTiles = 4;                 // 128-frame tiles per CTA
+constexpr int kPcFrames = 128 * kPcTiles;   // 512
+constexpr int kPcTaps = 4;                  // taps per weight stage
+constexpr int kPcMaxKp = 128;
+
+template <int CG>
+struct PcCfg {
+    static constexpr int kChunks = CG / 8;                  // 16-byte channel chunks
+    static constexpr int kWinRows = kPcFrames + kPcMaxKp;   // 640 (rows past Kp-1 unused)
+    static constexpr int kChunkA = kWinRows * 16;           // bytes per window chunk
+    static constexpr int kABytes = kChunks * kChunkA;
+    static constexpr int kTapBytes = CG * CG * 2;
+    static constexpr int kChunkB = CG * 16;
+    static constexpr int kStageBytes = kPcTaps * kTapBytes;
+    static constexpr int kStages = kStageBytes <= 20480 ? 4 : kStageBytes <= 32768 ? 3 : 2;
+    static constexpr int kSmem = kABytes + kStages * kStageBytes + 1024 + 128;
+    static constexpr int kTmemCols = kPcTiles * CG <= 128 ? 128 : kPcTiles * CG <= 256 ? 256 : 512;
+};
 
 struct PosConvArgs {
     float* out; const float* xin; const long long* off; const int* Tn;
-    int H, Kp, G, Cg, TC; const __half* wt; const float* bias;
+    int H, Kp, G; const __half* wt; const float* bias; int* err;
 };
 
 template <int CG>
-__global__ void __launch_bounds__(256)
-pos_conv_kernel(PosConvArgs a) {
-    constexpr int LDS = CG + 8;           // conflict-free ldmatrix row stride (halves)
-    constexpr int NT = CG / 8, KS = CG / 16;
-    extern __shared__ __align__(16) __half sm[];
+__global__ void __launch_bounds__(192, 1) pos_conv_tc_kernel(PosConvArgs a) {
+    using Cfg = PcCfg<CG>;
     const int u = blockIdx.z, g = blockIdx.y;
     const int T = a.Tn[u];
-    const int t0 = blockIdx.x * kPcRows;
+    const int t0 = blockIdx.x * kPcFrames;
     if (t0 >= T) return;
-    const int Kp = a.Kp, TC = a.TC, half = Kp / 2;
-    const int xrows = kPcRows + Kp;
-    __half* sX = sm;
-    __half* sW = sm + xrows * LDS;        // 2 chunks of TC*CG rows
-    const int chunk_elems = TC * CG * LDS;
+    const int n_tiles = min(kPcTiles, (T - t0 + 127) / 128);
+    const int Kp = a.Kp, half = Kp / 2;
     const long long base = a.off[u];
+    const int n_stages_total = Kp / kPcTaps;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + Cfg::kABytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + Cfg::kStages * Cfg::kStageBytes);
+    uint64_t* full = bars;                          // [kStages]
+    uint64_t* empty = bars + Cfg::kStages;          // [kStages]
+    uint64_t* a_ready = bars + 2 * Cfg::kStages;
+    uint64_t* acc_full = a_ready + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    auto load_w = [&](int chunk, int buf) {
-        const __half* src = a.wt + ((long long)g * Kp + (long long)chunk * TC) * CG * CG;
-        __half* dst = sW + buf * chunk_elems;
-        constexpr int CPR = CG / 8;      // 16-byte chunks per row
-        for (int i = threadIdx.x; i < TC * CG * CPR; i += blockDim.x) {
-            const int r = i / CPR, c = i % CPR;
-            cp_async16(smem_u32(dst + r * LDS + c * 8), src + (long long)r * CG + c * 8);
-        }
-    };
-    load_w(0, 0);
-    cp_async_commit();
-
-    // input window rows t0-half .. t0+kPcRows+half-1 (zero outside [0, T))
-    for (int i = threadIdx.x; i < xrows * (CG / 4); i += blockDim.x) {
-        const int r = i / (CG / 4), c4 = i % (CG / 4);
-        const int t = t0 - half + r;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t >= 0 && t < T) v = *reinterpret_cast<const float4*>(a.xin + (base + t) * a.H + g * CG + c4 * 4);
-        uint2 p;
-        p.x = pack_half2(v.x, v.y);
-        p.y = pack_half2(v.z, v.w);
-        *reinterpret_cast<uint2*>(sX + r * LDS + c4 * 4) = p;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::kStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(a_ready, 4);
+        mbar_init(acc_full, 1);
+        fence_mbar_init();
     }
+    if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
 
-    float acc[NT][4];
+    if (warp == 0) {
+        if (elect_one()) {
+            const uint8_t* wg = reinterpret_cast<const uint8_t*>(a.wt) + (size_t)g * Kp * Cfg::kTapBytes;
+            int stage = 0;
+            uint32_t phase = 0, issued = 0, last_par = 0;
+            for (int i = 0; i < n_stages_total; i++) {
+                if (!mbar_wait(&empty[stage], phase ^ 1u, a.err)) break;
+                mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+                bulk_load(sB + stage * Cfg::kStageBytes, wg + (size_t)i * Cfg::kStageBytes, Cfg::kStageBytes,
+                          &full[stage]);
+                issued |= 1u << stage;
+                last_par = (last_par & ~(1u << stage)) | (phase << stage);
+                if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+            }
+            for (int s = 0; s < Cfg::kStages; s++)
+                if (issued & (1u << s)) mbar_wait(&full[s], (last_par >> s) & 1u, a.err);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            constexpr uint32_t idesc = umma_idesc_f16(128, CG);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = mbar_wait(a_ready, 0, a.err);
+            for (int i = 0; i < n_stages_total && ok; i++) {
+                if (!mbar_wait(&full[stage], phase, a.err)) break;
+                tc_fence_after();
+                const uint32_t b_stage = smem_u32(sB + stage * Cfg::kStageBytes);
+                const uint32_t a0 = smem_u32(sA);
+                for (int tt = 0; tt < kPcTaps; tt++) {
+                    const int k = i * kPcTaps + tt;
 #pragma unroll
-    for (int i = 0; i < NT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+                    for (int s = 0; s < CG / 16; s++) {
+                        const uint64_t bd = umma_desc_noswz(b_stage + tt * Cfg::kTapBytes + 2 * s * Cfg::kChunkB,
+                                                            Cfg::kChunkB, 128);
+#pragma unroll
+                        for (int r = 0; r < kPcTiles; r++) {
+                            if (r < n_tiles) {
+                                const uint64_t ad =
+                                    umma_desc_noswz(a0 + 2 * s * Cfg::kChunkA + (r * 128 + k) * 16, Cfg::kChunkA, 128);
+                                umma_f16(tmem_base + (uint32_t)(r * CG), ad, bd, idesc, (k | s) != 0);
+                            }
+                        }
+                    }
+                }
+                umma_commit(&empty[stage]);
+                if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+            }
+            umma_commit(acc_full);   // also on error: completes once the issued MMAs have
+        }
+        __syncwarp();
+    } else {
+        // stage the input window: row w is frame t0 - Kp/2 + w, zero outside [0, T)
+        const int et = threadIdx.x - 64;                       // 0..127
+        const int rows = kPcFrames + Kp;
+        for (int i = et; i < rows * Cfg::kChunks; i += 128) {
+            const int w = i % rows, c = i / rows;
+            const int t = t0 - half + w;
+            uint4 p = make_uint4(0, 0, 0, 0);
+            if (t >= 0 && t < T) {
+                const float4* src = reinterpret_cast<const float4*>(a.xin + (base + t) * a.H + g * CG + c * 8);
+                const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
+                p.x = pack_half2(v0.x, v0.y);
+                p.y = pack_half2(v0.z, v0.w);
+                p.z = pack_half2(v1.x, v1.y);
+                p.w = pack_half2(v1.z, v1.w);
+            }
+            *reinterpret_cast<uint4*>(sA + c * Cfg::kChunkA + w * 16) = p;
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a_ready);
 
-    const int n_chunks = Kp / TC;
-    for (int ch = 0; ch < n_chunks; ch++) {
-        cp_async_wait<0>();
-        __syncthreads();
-        if (ch + 1 < n_chunks) load_w(ch + 1, (ch + 1) & 1);
-        cp_async_commit();
-        const __half* cw = sW + (ch & 1) * chunk_elems;
-        for (int tt = 0; tt < TC; tt++) {
-            const int tap = ch * TC + tt;
-            const __half* wtap = cw + tt * CG * LDS;
+        // epilogue: out = xin + gelu(acc + bias) for frames < T
+        const int q = warp & 3;
+        if (mbar_wait(acc_full, 0, a.err)) {
+            tc_fence_after();
+            const float* bias = a.bias + g * CG;
+            for (int r = 0; r < n_tiles; r++) {
+                const int t = t0 + r * 128 + q * 32 + lane;
+                const long long idx = (base + t) * a.H + g * CG;
 #pragma unroll
-            for (int ks = 0; ks < KS; ks++) {
-                uint32_t a0, a1, a2, a3;
-                const int xr = warp * 16 + (lane & 15) + tap;
-                ldsm_x4(smem_u32(sX + xr * LDS + ks * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
+                for (int c = 0; c < CG / 16; c++) {
+                    float v[16];
+                    tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(r * CG + c * 16), v);
+                    if (t < T) {
 #pragma unroll
-                for (int np = 0; np < NT / 2; np++) {
-                    const int co = np * 16 + (lane & 7) + ((lane >> 4) << 3);
-                    const int ci = ks * 16 + ((lane >> 3) & 1) * 8;
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4(smem_u32(wtap + co * LDS + ci), b0, b1, b2, b3);
-                    mma_16816(acc[2 * np], a0, a1, a2, a3, b0, b1);
-                    mma_16816(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
+                        for (int j = 0; j < 16; j += 4) {
+                            const float4 x = *reinterpret_cast<const float4*>(a.xin + idx + c * 16 + j);
+                            const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c * 16 + j));
+                            float4 o;
+                            o.x = x.x + gelu_tanh(v[j] + b.x);
+                            o.y = x.y + gelu_tanh(v[j + 1] + b.y);
+                            o.z = x.z + gelu_tanh(v[j + 2] + b.z);
+                            o.w = x.w + gelu_tanh(v[j + 3] + b.w);
+                            *reinterpret_cast<float4*>(a.out + idx + c * 16 + j) = o;
+                        }
+                    }
                 }
             }
         }
     }
-    // epilogue: out = x + gelu(conv + bias), rows < T
-    const int r0 = t0 + warp * 16 + (lane >> 2), r1 = r0 + 8;
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-        const int co = g * CG + nt * 8 + (lane & 3) * 2;
-        const float b0 = a.bias[co], b1 = a.bias[co + 1];
-        if (r0 < T) {
-            const long long idx = (base + r0) * a.H + co;
-            const float2 x = *reinterpret_cast<const float2*>(a.xin + idx);
-            *reinterpret_cast<float2*>(a.out + idx) =
-                make_float2(x.x + gelu_tanh(acc[nt][0] + b0), x.y + gelu_tanh(acc[nt][1] + b1));
-        }
-        if (r1 < T) {
-            const long long idx = (base + r1) * a.H + co;
-            const float2 x = *reinterpret_cast<const float2*>(a.xin + idx);
-            *reinterpret_cast<float2*>(a.out + idx) =
-                make_float2(x.x + gelu_tanh(acc[nt][2] + b0), x.y + gelu_tanh(acc[nt][3] + b1));
-        }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
     }
 }
 
 template <int CG>
-static int launch_pc(PosConvArgs a, int n_utt, int max_T, cudaStream_t st) {
-    // taps per weight chunk: a power of two dividing Kp, chunk <= 48 KB
-    int tc = 1;
-    while (tc * 2 <= a.Kp && a.Kp % (tc * 2) == 0 && (tc * 2) * CG * (CG + 8) * 2 <= 49152) tc *= 2;
-    a.TC = tc;
-    const size_t smem = ((size_t)(kPcRows + a.Kp) * (CG + 8) + 2 * (size_t)tc * CG * (CG + 8)) * 2;
-    if (smem > 227 * 1024) return W2V_ERR_ARGS;
-    if (cudaFuncSetAttribute(pos_conv_kernel<CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-        return W2V_ERR_LAUNCH;
-    dim3 grid((max_T + kPcRows - 1) / kPcRows, a.G, n_utt);
-    pos_conv_kernel<CG><<<grid, 256, smem, st>>>(a);
+static int launch_pc(const PosConvArgs& a, int n_utt, int max_T, cudaStream_t st) {
+    using Cfg = PcCfg<CG>;
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        if (cudaFuncSetAttribute(pos_conv_tc_kernel<CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
+            cudaSuccess)
+            return W2V_ERR_LAUNCH;
+        attr[dev & 63] = true;
+    }
+    dim3 grid((max_T + kPcFrames - 1) / kPcFrames, a.G, n_utt);
+    pos_conv_tc_kernel<CG><<<grid, 192, Cfg::kSmem, st>>>(a);
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
 }  // namespace w2v
 
 extern "C" int w2v_pos_conv(float* x, const float* xin, const long long* off, const int* T, int n_utt, int H,
-                            int Kp, int G, const void* wt, const float* bias, int max_T, void* stream) {
-    if (G <= 0 || H % G || Kp <= 0 || Kp % 2 || x == xin) return W2V_ERR_ARGS;
+                            int Kp, int G, const void* wt, const float* bias, int max_T, int* err, void* stream) {
+    if (G <= 0 || H % G || Kp <= 0 || Kp % w2v::kPcTaps || Kp > w2v::kPcMaxKp || x == xin) return W2V_ERR_ARGS;
+    if ((reinterpret_cast<uintptr_t>(wt) & 15) || (reinterpret_cast<uintptr_t>(xin) & 15) ||
+        (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(bias) & 15))
+        return W2V_ERR_ARGS;
     if (n_utt <= 0 || max_T <= 0) return W2V_OK;
-    w2v::PosConvArgs a{x, xin, off, T, H, Kp, G, H / G, 1, (const __half*)wt, bias};
+    w2v::PosConvArgs a{x, xin, off, T, H, Kp, G, (const __half*)wt, bias, err};
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     switch (H / G) {
         case 32: return w2v::launch_pc<32>(a, n_utt, max_T, st);
