@@ -79,14 +79,16 @@ int w2v_wave_stats(const float* audio, const long long* off, const int* len, int
  * waveform, then the layer's norm and GELU (src/wav2vec2.cpp:273-287,
  * src/ops.h:24-50,76-99).
  *   norm: 0 = none, 1 = GroupNorm over time per channel (needs gn_sums,
- *   a device double buffer [n_utt][C][2] that this call zeroes and fills),
- *   2 = LayerNorm over channels per frame.
+ *   a device double buffer [n_utt][C][2] used as scratch for the
+ *   statistics), 2 = LayerNorm over channels per frame.
  *   w0: fp32 [C][k0]; b0: fp32 [C] or NULL; gw/gb: fp32 [C] norm affine.
- *   out: fp16 [n_utt][rows_max][C]; frames per utterance (len-k0)/s0+1. */
+ *   out: fp16 [n_utt][rows_max][C]; frames per utterance (len-k0)/s0+1.
+ *   err: device word for bounded-wait failures of the tensor-core path
+ *   (k0 = 10, s0 = 5, C = 256 or 512, norm 0 or 1). */
 int w2v_conv0(const float* audio, const long long* off, const int* len, const int* frames, int n_utt,
               const float* stats, const float* w0, const float* b0, int C, int k0, int s0, int norm,
               const float* gw, const float* gb, double* gn_sums, void* out, long long rows_max,
-              int max_frames, void* stream);
+              int max_frames, int* err, void* stream);
 
 /* w2v_conv0 for callers that cannot allocate device memory.  No counterpart
  * in the reference (which has no GPU code): same arguments and result as
@@ -101,7 +103,7 @@ int w2v_conv0(const float* audio, const long long* off, const int* len, const in
 int w2v_conv0_noalloc(const float* audio, const long long* off, const int* len, const int* frames,
                       int n_utt, const float* stats, const float* w0, const float* b0, int C, int k0,
                       int s0, int norm, const float* gw, const float* gb, void* out, long long rows_max,
-                      int max_frames, void* stream);
+                      int max_frames, int* err, void* stream);
 
 /* Row LayerNorm (eps 1e-5, src/ops.h:24-36) over D columns of fp16 or fp32
  * rows, optional GELU after the affine, fp32 and/or fp16 outputs.

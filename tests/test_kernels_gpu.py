@@ -226,13 +226,16 @@ def test_conv0_norm_gelu(K, synth, norm):
     gn = torch.empty(len(lens) * C * 2, device="cuda", dtype=torch.float64)
     rows = int(frames.max()) + 5
     out = torch.zeros(len(lens), rows, C, device="cuda", dtype=torch.float16)
+    err = err_word()
     K.wave_stats(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), len(lens), stats.data_ptr(), stream())
     K.conv0(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), d_fr.data_ptr(), len(lens), stats.data_ptr(),
             d_w0.data_ptr(), d_b0.data_ptr(), C, k0, s0, norm,
             d_gw.data_ptr() if norm else 0, d_gb.data_ptr() if norm else 0,
-            gn.data_ptr() if norm == 1 else 0, out.data_ptr(), rows, int(frames.max()), stream())
+            gn.data_ptr() if norm == 1 else 0, out.data_ptr(), rows, int(frames.max()), err.data_ptr(), stream())
     torch.cuda.synchronize()
+    assert int(err.item()) == 0
     got = out.float().cpu().numpy()
+    assert (got[:, int(frames.max()):] == 0).all(), "rows past the frames were written"
     for u, x in enumerate(audio):
         xd = x.astype(np.float64)
         xn = ((x - np.float32(xd.mean())) * np.float32(1 / np.sqrt(np.float32(xd.var()) + 1e-7))).astype(np.float32)

@@ -43,14 +43,14 @@ def test_conv0_noalloc_matches_allocating_entry_point(pkg, synth):
     ref = torch.zeros(len(lens), rows, C, device="cuda", dtype=torch.float16)
     assert L.w2v_conv0(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), d_fr.data_ptr(), len(lens),
                        stats.data_ptr(), d_w0.data_ptr(), None, C, k0, s0, norm, d_gw.data_ptr(), d_gb.data_ptr(),
-                       gn.data_ptr(), ref.data_ptr(), rows, rows, st) == 0
+                       gn.data_ptr(), ref.data_ptr(), rows, rows, None, st) == 0
     torch.cuda.synchronize()
     ref = ref.float()
     for call in range(2):
         out = torch.full((len(lens), rows, C), float("nan"), device="cuda", dtype=torch.float16)
         rc = L.w2v_conv0_noalloc(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), d_fr.data_ptr(),
                                  len(lens), stats.data_ptr(), d_w0.data_ptr(), None, C, k0, s0, norm,
-                                 d_gw.data_ptr(), d_gb.data_ptr(), out.data_ptr(), rows, rows, st)
+                                 d_gw.data_ptr(), d_gb.data_ptr(), out.data_ptr(), rows, rows, None, st)
         assert rc == 0, f"call {call}: status {rc}"
         torch.cuda.synchronize()
         for u, f in enumerate(frames):
@@ -67,8 +67,8 @@ def test_conv0_noalloc_rejects_oversized_requests(pkg):
     L = b.lib()
     # 65 utterances exceed the built-in buffer: rejected before anything is launched
     rc = L.w2v_conv0_noalloc(None, None, None, None, 65, None, None, None, 512, 10, 5, 1, None, None, None, 1, 1,
-                             None)
+                             None, None)
     assert rc == W2V_ERR_CAPACITY
     rc = L.w2v_conv0_noalloc(None, None, None, None, 4, None, None, None, 1024, 10, 5, 1, None, None, None, 1, 1,
-                             None)
+                             None, None)
     assert rc == W2V_ERR_CAPACITY

@@ -63,9 +63,9 @@ SIGNATURES = {
     "w2v_dequant_f16": (_i, [_vp, _i, _ll, _ll, _vp, _vp]),
     "w2v_wave_stats": (_i, [_vp, _vp, _vp, _i, _vp, _vp]),
     "w2v_conv0": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _ll, _i,
-                       _vp]),
+                       _vp, _vp]),
     "w2v_conv0_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _ll, _i,
-                               _vp]),
+                               _vp, _vp]),
     "w2v_layer_norm": (_i, [_vp, _i, _ll, _ll, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _ll, _vp]),
     "w2v_pos_conv": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _i, _vp, _vp]),
     "w2v_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _ll, _vp, _vp]),
@@ -265,9 +265,9 @@ class kernels:
 
     @staticmethod
     def conv0(audio, off, length, frames, n_utt, stats, w0, b0, Cc, k0, s0, norm, gw, gb, gn, out, rows_max,
-              max_frames, stream=0):
+              max_frames, err=0, stream=0):
         kernels.check(lib().w2v_conv0(audio, off, length, frames, n_utt, stats, w0, b0 or None, Cc, k0, s0, norm,
-                                      gw or None, gb or None, gn or None, out, rows_max, max_frames,
+                                      gw or None, gb or None, gn or None, out, rows_max, max_frames, err or None,
                                       stream or None), "w2v_conv0")
 
     @staticmethod

@@ -482,7 +482,7 @@ void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, 
                          c.conv_bias[0] ? conv_b_[0].as<float>() : nullptr, C, c.conv_k[0], c.conv_s[0], norm0,
                          c.conv_norm[0] ? conv_gw_[0].as<float>() : nullptr,
                          c.conv_norm[0] ? conv_gb_[0].as<float>() : nullptr, gn_.as<double>(), actA_.p, g.R[0],
-                         g.Lmax[0], st);
+                         g.Lmax[0], err_.as<int>(), st);
     });
     if (norm0 == 1) launches_cur_++;   // the GroupNorm statistics pass is a second kernel
     // 2. conv layers 1..n-1 as implicit GEMMs over the strided windows

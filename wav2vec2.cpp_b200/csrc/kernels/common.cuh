@@ -443,3 +443,20 @@ W2V_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 }  // namespace w2v
+
+namespace w2v {
+// Per-warp 32 x 32 fp32 transpose through a private 4 KB shared buffer:
+// stage_put writes a row per lane (float4 groups XOR-swizzled by row, so
+// both this and the reads below are bank-conflict free); stage_get then reads
+// row r, column group cg (4 floats), letting a warp work on 4 rows x 32
+// columns per instruction (thread t: column group t%8 of rows t/8 + 4i).
+W2V_DEV void stage_put(float* stg, const float (&v)[32]) {
+    const int lane = threadIdx.x & 31;
+    float4* row = reinterpret_cast<float4*>(stg + lane * 32);
+#pragma unroll
+    for (int j = 0; j < 8; j++) row[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+W2V_DEV float4 stage_get(const float* stg, int r, int cg) {
+    return reinterpret_cast<const float4*>(stg + r * 32)[cg ^ (r & 7)];
+}
+}  // namespace w2v

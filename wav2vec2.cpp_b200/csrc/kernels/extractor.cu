@@ -4,6 +4,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "conv0_tc.cuh"
 #include "w2v_kernels.h"
 
 namespace w2v {
@@ -169,9 +170,12 @@ __global__ void __launch_bounds__(kGramThreads) conv0_gram_kernel(const float* _
 
 // Per (utterance, channel) GroupNorm mean and 1/sqrt(var + 1e-5) from the
 // window moments; `stats` holds the (mu, r) the conv kernel normalises with.
+// With gw/gb given, writes the channel's full affine instead: (scale, shift)
+// with GroupNorm(b + conv) = conv * scale + shift.
 __global__ void conv0_gram_finalize_kernel(const double* __restrict__ part, int chunks,
                                            const float* __restrict__ stats, const int* __restrict__ frames,
                                            const float* __restrict__ w0, const float* __restrict__ b0, int C,
+                                           const float* __restrict__ gw, const float* __restrict__ gb,
                                            float2* __restrict__ gnf) {
     __shared__ double m[kGramN];
     __shared__ double Sn[kGramK];
@@ -212,6 +216,11 @@ __global__ void conv0_gram_finalize_kernel(const double* __restrict__ part, int 
             const double ey2 = (Fd * b * b + 2.0 * b * ws + wgw) / Fd;
             const float var = (float)fmax(ey2 - mean * mean, 0.0);
             o = make_float2((float)mean, 1.f / sqrtf(var + 1e-5f));
+        }
+        if (gw) {
+            const float sc = o.y * __ldg(gw + c);
+            const float bc = b0 ? __ldg(b0 + c) : 0.f;
+            o = make_float2(sc, __ldg(gb + c) + (bc - o.x) * sc);
         }
         gnf[(long long)u * C + c] = o;
     }
@@ -775,7 +784,7 @@ extern "C" int w2v_wave_stats(const float* audio, const long long* off, const in
 extern "C" int w2v_conv0(const float* audio, const long long* off, const int* len, const int* frames, int n_utt,
                          const float* stats, const float* w0, const float* b0, int C, int k0, int s0, int norm,
                          const float* gw, const float* gb, double* gn_sums, void* out, long long rows_max,
-                         int max_frames, void* stream) {
+                         int max_frames, int* err, void* stream) {
     if (C > 512 || C % 2 || k0 > kC0MaxK || k0 <= 0 || s0 <= 0 || norm < 0 || norm > 2) return W2V_ERR_ARGS;
     if ((norm == 1 && !gn_sums) || (norm && (!gw || !gb))) return W2V_ERR_ARGS;
     if (n_utt <= 0 || max_frames <= 0) return W2V_OK;
@@ -796,11 +805,18 @@ extern "C" int w2v_conv0(const float* audio, const long long* off, const int* le
                                                                                         part);
                 int rc = launch_rc();
                 if (rc) return rc;
+                const bool tc = conv0_tc_supported(C, k0, s0, norm, out);
                 conv0_gram_finalize_kernel<<<n_utt, 512, 0, S(stream)>>>(part, chunks, stats, frames, w0, b0, C,
-                                                                         gnf);
+                                                                         tc ? gw : nullptr, tc ? gb : nullptr, gnf);
                 rc = launch_rc();
                 if (rc) return rc;
                 a.gnf = gnf;
+                if (tc) {
+                    // tensor-core conv + GroupNorm affine + GELU
+                    Conv0TcArgs t{audio, off, frames, stats, w0, b0, C, norm, gw, gb, gnf, (__half*)out, rows_max,
+                                  n_utt, (max_frames + 127) / 128, err};
+                    return launch_conv0_tc(t, S(stream));
+                }
             } else {
                 if (cudaMemsetAsync(gn_sums, 0, sizeof(double) * 2 * C * (size_t)n_utt, S(stream)) != cudaSuccess)
                     return W2V_ERR_LAUNCH;
@@ -918,7 +934,7 @@ int scratch_address(double** out) {
 extern "C" int w2v_conv0_noalloc(const float* audio, const long long* off, const int* len, const int* frames,
                                  int n_utt, const float* stats, const float* w0, const float* b0, int C, int k0,
                                  int s0, int norm, const float* gw, const float* gb, void* out, long long rows_max,
-                                 int max_frames, void* stream) {
+                                 int max_frames, int* err, void* stream) {
     double* gn = nullptr;
     if (norm == 1) {
         if (n_utt > kNoAllocMaxUtt || C > kNoAllocMaxChannels) return W2V_ERR_CAPACITY;
@@ -927,5 +943,5 @@ extern "C" int w2v_conv0_noalloc(const float* audio, const long long* off, const
     }
     // w2v_conv0 zeroes the statistics before accumulating into them.
     return w2v_conv0(audio, off, len, frames, n_utt, stats, w0, b0, C, k0, s0, norm, gw, gb, gn, out, rows_max,
-                     max_frames, stream);
+                     max_frames, err, stream);
 }

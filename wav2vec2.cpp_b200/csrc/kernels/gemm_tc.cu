@@ -137,17 +137,6 @@ W2V_DEV void epilogue_chunk(const GemmParams& p, long long out_row, long long re
 // reads are both bank-conflict free) and then works on 4 rows x 32 columns
 // per instruction: thread t owns column group t%8 of rows t/8 + 4i.
 
-W2V_DEV void stage_put(float* stg, const float (&v)[32]) {
-    const int lane = threadIdx.x & 31;
-    float4* row = reinterpret_cast<float4*>(stg + lane * 32);
-#pragma unroll
-    for (int j = 0; j < 8; j++) row[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-}
-
-W2V_DEV float4 stage_get(const float* stg, int r, int cg) {
-    return reinterpret_cast<const float4*>(stg + r * 32)[cg ^ (r & 7)];
-}
-
 // Residual of this thread's 8 (row, 4-column) cells of a chunk; rows past
 // m_valid and columns past N read as zero.
 W2V_DEV void load_resid_t(const GemmParams& p, long long out_row0, int row0, int col0, float4 (&res)[8]) {
