@@ -213,35 +213,18 @@ W2V_DEV bool elect_one() {
 // ── numerics ────────────────────────────────────────────────────────────────
 // The reference's tanh-approximation GELU (ops.h:18-21),
 //   0.5 x (1 + tanh(u)),  u = 0.7978845608 (x + 0.044715 x^3),
-// evaluated through the identity 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)):
-// one exp2 and one reciprocal on the special-function unit, relative error
-// ~1e-6 (well below the fp16 rounding of every output it feeds).  Limits:
-// x -> -inf gives -0 (exp overflows to inf), x -> +inf gives x.
-//
-// 2^z on the FMA pipe, for kernels whose special-function unit is saturated:
-// Cody-Waite range reduction z = n + f, |f| <= 1/2, with n obtained by the
-// round-to-nearest trick (adding 1.5 * 2^23), then the degree-6 Taylor
-// polynomial of 2^f = e^(f ln 2) (truncation error <= (ln2 / 2)^7 / 7! ~ 1.2e-7
-// relative) and 2^n applied by adding n to the exponent field.  z is clamped
-// to [-126, 126] so the result stays a normal float.
-W2V_DEV float exp2_fma(float z) {
-    z = fminf(fmaxf(z, -126.0f), 126.0f);
-    const float t = z + 12582912.0f;                       // 1.5 * 2^23: rounds z to an integer
-    const int n = __float_as_int(t) - 0x4B400000;          // that integer, from the mantissa bits
-    const float f = z - (t - 12582912.0f);
-    float p = 1.5403530393381606e-4f;                      // (ln 2)^6 / 720
-    p = fmaf(p, f, 1.3333558146428443e-3f);                // (ln 2)^5 / 120
-    p = fmaf(p, f, 9.6181291076284772e-3f);                // (ln 2)^4 / 24
-    p = fmaf(p, f, 5.5504108664821580e-2f);                // (ln 2)^3 / 6
-    p = fmaf(p, f, 0.24022650695910071f);                  // (ln 2)^2 / 2
-    p = fmaf(p, f, 0.69314718055994531f);                  // ln 2
-    p = fmaf(p, f, 1.0f);
-    return __int_as_float(__float_as_int(p) + (n << 23));
-}
-
+// evaluated through 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)) with the
+// constants folded into the exponent: -2 u log2(e) = x (A + B x^2),
+// A = -2 sqrt(2/pi) log2(e), B = 0.044715 A.  Five FMA-pipe operations plus
+// ex2 and rcp on the special-function unit; within 1e-6 of the tanh form
+// (well below the fp16 rounding of every output it feeds).  x -> -inf gives
+// -0 (the power overflows to inf), x -> +inf gives x.
 W2V_DEV float gelu_tanh(float x) {
-    const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-    return __fdividef(x, 1.0f + __expf(-2.0f * u));
+    const float z = x * fmaf(x * x, -0.10294324f, -2.3022082f);
+    float e, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(z));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+    return x * r;
 }
 
 W2V_DEV uint32_t pack_half2(float a, float b) {

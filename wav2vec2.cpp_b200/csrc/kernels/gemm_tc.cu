@@ -685,7 +685,7 @@ static int pick_bn(int N, int m_valid, int n_batch, long long K, int epilogue) {
     const int sms = sm_count();
     const long long mt1 = (long long)((m_valid + kBM - 1) / kBM) * n_batch;
     const long long mt2 = (long long)((m_valid + 2 * kBM - 1) / (2 * kBM)) * n_batch;
-    const double E = epilogue == W2V_EPI_F16 ? 293 : epilogue == W2V_EPI_F16_GELU ? 589
+    const double E = epilogue == W2V_EPI_F16 ? 293 : epilogue == W2V_EPI_F16_GELU ? 442
                    : epilogue == W2V_EPI_F32 ? 450 : 932;
     int best = 64;
     double best_cost = 1e300;
