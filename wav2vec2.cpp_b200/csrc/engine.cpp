@@ -1,8 +1,10 @@
 #include "engine.hpp"
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <stdexcept>
 #include <thread>
 
@@ -168,6 +170,8 @@ Engine::Engine(const GgufFile& gf, const ModelConfig& cfg, int device) : cfg_(cf
     cuda_check(cudaSetDevice(device_), "cudaSetDevice");
     cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
     cuda_check(cudaEventCreateWithFlags(&meta_done_, cudaEventDisableTiming), "cudaEventCreate");
+    cuda_check(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    for (auto& e : chunk_ev_) cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
     err_.ensure(sizeof(int));
     // Every transfer of the engine is ordered on its own (non-blocking) stream:
     // a legacy-stream cudaMemcpy from pageable memory may return before its DMA
@@ -180,6 +184,7 @@ Engine::Engine(const GgufFile& gf, const ModelConfig& cfg, int device) : cfg_(cf
 Engine::~Engine() {
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    if (copy_stream_) cudaStreamSynchronize(copy_stream_);
     auto rel = [](DevBuf& b) { b.release(); };
     for (DevBuf* b : {&conv0_w_, &conv0_b_, &proj_lnw_, &proj_lnb_, &proj_w_, &proj_b_, &pos_w_, &pos_b_, &enc_lnw_,
                       &enc_lnb_, &lm_w_, &lm_b_, &audio_stage_, &meta_, &stats_, &gn_, &actA_, &actB_, &feat_,
@@ -195,6 +200,9 @@ Engine::~Engine() {
     prof_fold();
     for (auto e : ev_pool_) cudaEventDestroy(e);
     if (meta_done_) cudaEventDestroy(meta_done_);
+    for (auto e : chunk_ev_)
+        if (e) cudaEventDestroy(e);
+    if (copy_stream_) cudaStreamDestroy(copy_stream_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -431,23 +439,73 @@ int Engine::check_device_error() {
 
 // ── forward ─────────────────────────────────────────────────────────────────
 
-void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, float* dbg_feat, float* dbg_stages) {
-    if (!st) st = stream_;
+bool Engine::fwd_begin(const BatchGeom& g, cudaStream_t st) {
     cuda_check(cudaSetDevice(device_), "cudaSetDevice");
-    const ModelConfig& c = cfg_;
-    const int B = g.n_utt, C = c.conv_dim, H = c.hidden, F = c.ffn, V = c.vocab;
     last_M_ = g.M;
     launches_cur_ = 0;
-    if (B == 0) { launches_last_ = 0; return; }
+    if (g.n_utt == 0) { launches_last_ = 0; return false; }
     ensure_workspace(g);
     upload_meta(g, st);
+    if (g.M == 0) {
+        cuda_check(cudaMemsetAsync(nspans_.p, 0, sizeof(int) * g.n_utt, st), "memset");
+        launches_last_ = 0;
+        return false;
+    }
+    return true;
+}
+
+void Engine::fwd_extract(const float* d_audio, const BatchGeom& g, int u0, int u1, cudaStream_t st) {
+    const ModelConfig& c = cfg_;
+    const int n = u1 - u0, C = c.conv_dim;
+    if (n <= 0) return;
+    int* err = err_.as<int>();
+    // 1. waveform normalisation statistics + conv layer 0 with its norm and GELU
+    launch(P_WAVE, 0.0, st, "wave_stats", [&] {
+        return w2v_wave_stats(d_audio, d_audio_off_ + u0, d_len_ + u0, n, stats_.as<float>() + 2 * u0, st);
+    });
+    const int norm0 = c.conv_norm[0] ? (c.group_norm ? 1 : 2) : 0;
+    long long f0 = 0;
+    for (int u = u0; u < u1; u++) f0 += g.L[0][u];
+    uint16_t* actA = actA_.as<uint16_t>();
+    uint16_t* actB = actB_.as<uint16_t>();
+    launch(P_CONV0, 2.0 * f0 * C * c.conv_k[0] * (norm0 == 1 ? 2 : 1), st, "conv0", [&] {
+        return w2v_conv0(d_audio, d_audio_off_ + u0, d_len_ + u0, d_L_[0] + u0, n, stats_.as<float>() + 2 * u0,
+                         conv0_w_.as<float>(), c.conv_bias[0] ? conv_b_[0].as<float>() : nullptr, C, c.conv_k[0],
+                         c.conv_s[0], norm0, c.conv_norm[0] ? conv_gw_[0].as<float>() : nullptr,
+                         c.conv_norm[0] ? conv_gb_[0].as<float>() : nullptr, gn_.as<double>(),
+                         actA + (size_t)u0 * g.R[0] * C, g.R[0], g.Lmax[0], err, st);
+    });
+    if (norm0 == 1) launches_cur_ += 2;   // window moments and their reduction are two more kernels
+    // 2. conv layers 1..n-1 as implicit GEMMs over the strided windows
+    uint16_t* cur = actA;
+    uint16_t* nxt = actB;
+    for (int i = 1; i < c.n_conv; i++) {
+        const bool ln = c.conv_norm[i];
+        long long rows = 0;
+        for (int u = u0; u < u1; u++) rows += g.L[i][u];
+        uint16_t* in = cur + (size_t)u0 * g.R[i - 1] * C;
+        uint16_t* out = nxt + (size_t)u0 * g.R[i] * C;
+        if (g.Lmax[i] > 0)
+            launch(P_GEMM_CONV, 2.0 * rows * C * C * c.conv_k[i], st, "gemm", [&] {
+                return w2v_gemm_f16(in, C, c.conv_k[i], c.conv_s[i], C, g.R[i - 1], n, g.R[i - 1] * C,
+                                    conv_w_[i].p, C, out, C, g.R[i], g.Lmax[i],
+                                    c.conv_bias[i] ? conv_b_[i].as<float>() : nullptr, nullptr, C,
+                                    ln ? W2V_EPI_F16 : W2V_EPI_F16_GELU, 0, err, st);
+            });
+        if (ln)
+            launch(P_LN, 0.0, st, "conv layer_norm", [&] {
+                return w2v_layer_norm(out, 1, C, g.R[i], d_L_[i] + u0, nullptr, n, 0, C, conv_gw_[i].as<float>(),
+                                      conv_gb_[i].as<float>(), 1, nullptr, out, C, st);
+            });
+        std::swap(cur, nxt);
+    }
+}
+
+void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, float* dbg_stages) {
+    const ModelConfig& c = cfg_;
+    const int B = g.n_utt, C = c.conv_dim, H = c.hidden, F = c.ffn, V = c.vocab;
     int* err = err_.as<int>();
     const long long M = g.M;
-    if (M == 0) {
-        cuda_check(cudaMemsetAsync(nspans_.p, 0, sizeof(int) * B, st), "memset");
-        launches_last_ = 0;
-        return;
-    }
     auto gemm = [&](int cat, const void* A, long long cin, int taps, int stride, long long row_stride,
                     long long rows_in, long long batches, long long batch_stride, const void* W, int N, void* out,
                     long long ldc, long long c_batch_rows, int m_valid, const void* bias, const float* resid, int epi,
@@ -468,41 +526,8 @@ void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, 
                    "debug copy");
         cuda_check(cudaStreamSynchronize(st), "debug copy");
     };
-    long long n_audio = 0;
-    for (int u = 0; u < B; u++) n_audio += g.n_samples[u];
-
-    // 1. waveform normalisation statistics + conv layer 0 with its norm and GELU
-    launch(P_WAVE, 0.0, st, "wave_stats",
-           [&] { return w2v_wave_stats(d_audio, d_audio_off_, d_len_, B, stats_.as<float>(), st); });
-    const int norm0 = c.conv_norm[0] ? (c.group_norm ? 1 : 2) : 0;
-    long long f0 = 0;
-    for (int u = 0; u < B; u++) f0 += g.L[0][u];
-    launch(P_CONV0, 2.0 * f0 * C * c.conv_k[0] * (norm0 == 1 ? 2 : 1), st, "conv0", [&] {
-        return w2v_conv0(d_audio, d_audio_off_, d_len_, d_L_[0], B, stats_.as<float>(), conv0_w_.as<float>(),
-                         c.conv_bias[0] ? conv_b_[0].as<float>() : nullptr, C, c.conv_k[0], c.conv_s[0], norm0,
-                         c.conv_norm[0] ? conv_gw_[0].as<float>() : nullptr,
-                         c.conv_norm[0] ? conv_gb_[0].as<float>() : nullptr, gn_.as<double>(), actA_.p, g.R[0],
-                         g.Lmax[0], err_.as<int>(), st);
-    });
-    if (norm0 == 1) launches_cur_++;   // the GroupNorm statistics pass is a second kernel
-    // 2. conv layers 1..n-1 as implicit GEMMs over the strided windows
-    void* cur = actA_.p;
-    void* nxt = actB_.p;
-    for (int i = 1; i < c.n_conv; i++) {
-        const bool ln = c.conv_norm[i];
-        long long rows = 0;
-        for (int u = 0; u < B; u++) rows += g.L[i][u];
-        if (g.Lmax[i] > 0)
-            gemm(P_GEMM_CONV, cur, C, c.conv_k[i], c.conv_s[i], C, g.R[i - 1], B, g.R[i - 1] * C, conv_w_[i].p, C, nxt,
-                 C, g.R[i], g.Lmax[i], c.conv_bias[i] ? conv_b_[i].p : nullptr, nullptr,
-                 ln ? W2V_EPI_F16 : W2V_EPI_F16_GELU, 2.0 * rows * C * C * c.conv_k[i]);
-        if (ln)
-            launch(P_LN, 0.0, st, "conv layer_norm", [&] {
-                return w2v_layer_norm(nxt, 1, C, g.R[i], d_L_[i], nullptr, B, 0, C, conv_gw_[i].as<float>(),
-                                      conv_gb_[i].as<float>(), 1, nullptr, nxt, C, st);
-            });
-        std::swap(cur, nxt);
-    }
+    // output of the last conv layer: the ping-pong buffers alternate once per layer
+    const void* cur = (c.n_conv - 1) % 2 ? actB_.p : actA_.p;
     if (dbg_feat) {
         std::vector<uint16_t> tmp((size_t)g.T[0] * C);
         cuda_check(cudaMemcpyAsync(tmp.data(), cur, tmp.size() * 2, cudaMemcpyDeviceToHost, st), "debug copy");
@@ -521,7 +546,7 @@ void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, 
     float* x = x_.as<float>();
     launch(P_POSCONV, 2.0 * M * c.pos_k * (H / c.pos_g) * H, st, "pos_conv", [&] {
         return w2v_pos_conv(x, pbuf_.as<float>(), d_T_off_, d_T_, B, H, c.pos_k, c.pos_g, pos_w_.p,
-                            pos_b_.as<float>(), g.T_max, err_.as<int>(), st);
+                            pos_b_.as<float>(), g.T_max, err, st);
     });
     const int n_heads = c.n_heads;
     double attn_flops = 0;
@@ -574,9 +599,16 @@ void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, 
         return w2v_ctc_greedy(logits_.as<float>(), d_T_off_, d_T_, B, V, ids_.as<int>(), spans_.as<int>(),
                               nspans_.as<int>(), g.T_max, st);
     });
-    (void)n_audio;
     launches_last_ = launches_cur_;
 }
+
+void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, float* dbg_feat, float* dbg_stages) {
+    if (!st) st = stream_;
+    if (!fwd_begin(g, st)) return;
+    fwd_extract(d_audio, g, 0, g.n_utt, st);
+    fwd_encode(g, st, dbg_feat, dbg_stages);
+}
+
 
 void Engine::run_host(const std::vector<const float*>& audio, const std::vector<int>& n_samples,
                       std::vector<float>* logits, std::vector<int>* spans, std::vector<int>* n_spans,
@@ -592,33 +624,54 @@ void Engine::run_host(const std::vector<const float*>& audio, const std::vector<
         h_audio_n_ = total;
     }
     audio_stage_.ensure(std::max<size_t>(total, 1) * sizeof(float));
-    // Pack the caller's (pageable) utterances into pinned staging on several
-    // host threads; each thread uploads its contiguous range as soon as it is
-    // packed, so the host copies overlap the DMA of earlier ranges.
+    // Pipelined upload: the batch is cut into up to kMaxChunks utterance
+    // chunks.  Host threads pack the caller's (pageable) utterances into
+    // pinned staging chunk by chunk; as soon as a chunk is packed it is copied
+    // on the copy stream and the feature extractor for its utterances is
+    // queued behind that copy, so the DMA and packing of later chunks overlap
+    // the convolutions of earlier ones.  The encoder then runs on the batch.
+    const int B = g.n_utt;
+    const int nch = B >= 32 ? kMaxChunks : B >= 8 ? 2 : 1;
+    std::vector<int> cu(nch + 1);
+    for (int k = 0; k <= nch; k++) cu[k] = (int)((long long)B * k / nch);
     const int hw = (int)std::max(1u, std::thread::hardware_concurrency());
-    const int nt = std::max(1, std::min({8, hw / 2, g.n_utt}));
-    std::vector<std::thread> packers;
-    std::vector<int> rc(nt, 0);
+    const int nt = std::max(1, std::min({8, hw / 2, std::max(1, B / nch)}));
+    std::unique_ptr<std::atomic<int>[]> packed(new std::atomic<int>[nch]);
+    for (int k = 0; k < nch; k++) packed[k].store(0);
     auto pack = [&](int t) {
-        const int u0 = (int)((long long)g.n_utt * t / nt), u1 = (int)((long long)g.n_utt * (t + 1) / nt);
-        if (u0 >= u1) return;
-        if (cudaSetDevice(device_) != cudaSuccess) { rc[t] = 1; return; }   // the runtime's device is per thread
-        for (int u = u0; u < u1; u++)
-            if (n_samples[u]) memcpy(h_audio_ + g.audio_off[u], audio[u], (size_t)n_samples[u] * sizeof(float));
-        const long long b0 = g.audio_off[u0], b1 = g.audio_off[u1 - 1] + n_samples[u1 - 1];
-        if (b1 > b0)
-            rc[t] = cudaMemcpyAsync(audio_stage_.as<float>() + b0, h_audio_ + b0, (size_t)(b1 - b0) * sizeof(float),
-                                    cudaMemcpyHostToDevice, stream_) != cudaSuccess;
+        for (int k = 0; k < nch; k++) {
+            const int n = cu[k + 1] - cu[k];
+            const int u0 = cu[k] + (int)((long long)n * t / nt), u1 = cu[k] + (int)((long long)n * (t + 1) / nt);
+            for (int u = u0; u < u1; u++)
+                if (n_samples[u]) memcpy(h_audio_ + g.audio_off[u], audio[u], (size_t)n_samples[u] * sizeof(float));
+            packed[k].fetch_add(1, std::memory_order_release);
+        }
     };
-    if (nt == 1) {
-        pack(0);
-    } else {
+    if (fwd_begin(g, stream_)) {
+        std::vector<std::thread> packers;
+        struct Joiner {
+            std::vector<std::thread>& v;
+            ~Joiner() {
+                for (auto& t : v)
+                    if (t.joinable()) t.join();
+            }
+        } joiner{packers};
         for (int t = 0; t < nt; t++) packers.emplace_back(pack, t);
-        for (auto& th : packers) th.join();
+        for (int k = 0; k < nch; k++) {
+            while (packed[k].load(std::memory_order_acquire) < nt) std::this_thread::yield();
+            const long long b0 = g.audio_off[cu[k]];
+            const long long b1 = g.audio_off[cu[k + 1] - 1] + n_samples[cu[k + 1] - 1];
+            if (b1 > b0)
+                cuda_check(cudaMemcpyAsync(audio_stage_.as<float>() + b0, h_audio_ + b0,
+                                           (size_t)(b1 - b0) * sizeof(float), cudaMemcpyHostToDevice, copy_stream_),
+                           "audio upload");
+            cuda_check(cudaEventRecord(chunk_ev_[k], copy_stream_), "chunk event");
+            cuda_check(cudaStreamWaitEvent(stream_, chunk_ev_[k], 0), "chunk wait");
+            fwd_extract(audio_stage_.as<float>(), g, cu[k], cu[k + 1], stream_);
+        }
+        for (auto& t : packers) t.join();
+        fwd_encode(g, stream_, nullptr, nullptr);
     }
-    for (int r : rc)
-        if (r) throw std::runtime_error("audio upload failed");
-    forward(audio_stage_.as<float>(), g, stream_);
     if (g.M > 0) {
         if (logits) {
             logits->resize((size_t)g.M * cfg_.vocab);

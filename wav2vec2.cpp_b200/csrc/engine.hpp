@@ -109,6 +109,13 @@ private:
                        size_t row_offset = 0);
     void ensure_workspace(const BatchGeom& g);
     void upload_meta(const BatchGeom& g, cudaStream_t st);
+    // The forward in three parts: begin (workspace, metadata; false if there
+    // is nothing to compute), the feature extractor for utterances [u0, u1)
+    // (waveform statistics, conv layers; utterances are independent there),
+    // and everything after it over the whole batch.
+    bool fwd_begin(const BatchGeom& g, cudaStream_t st);
+    void fwd_extract(const float* d_audio, const BatchGeom& g, int u0, int u1, cudaStream_t st);
+    void fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, float* dbg_stages);
     // Launch bookkeeping: counts the launch and, when profiling, brackets it
     // with events attributed to category `cat` with `flops` algorithmic FLOPs.
     template <typename Fn> void launch(int cat, double flops, cudaStream_t st, const char* what, Fn fn);
@@ -149,6 +156,10 @@ private:
     size_t h_audio_n_ = 0;
     std::vector<uint8_t> meta_host_;
     cudaEvent_t meta_done_ = nullptr;
+    // host-batch uploads: a copy stream and one event per utterance chunk
+    static constexpr int kMaxChunks = 4;
+    cudaStream_t copy_stream_ = nullptr;
+    cudaEvent_t chunk_ev_[kMaxChunks] = {};
 
     // device pointers into meta_
     long long* d_audio_off_ = nullptr;
