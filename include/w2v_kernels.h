@@ -35,6 +35,7 @@ enum {
     W2V_EPI_F16_GELU = 1,   /* C(fp16) = gelu_tanh(acc + bias)   */
     W2V_EPI_F32 = 2,        /* C(fp32) = acc + bias              */
     W2V_EPI_F32_RESID = 3,  /* C(fp32) = acc + bias + resid      */
+    W2V_EPI_F32_RESID_LN = 4, /* C(fp32) = acc + bias + LayerNorm(resid) (w2v_gemm_f16_ln_resid) */
 };
 
 /* tcgen05 GEMM, C = epi(A . B^T).  Replaces ggml_mul_mat in
@@ -56,6 +57,18 @@ int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_stride, long 
                  int N, void* C, long long ldc, long long c_batch_rows, int m_valid, const float* bias,
                  const float* resid, long long ldr, int epilogue, int block_n, int* err,
                  void* stream);
+
+/* w2v_gemm_f16 with the W2V_EPI_F32_RESID_LN epilogue: the residual rows are
+ * the raw input of a LayerNorm (src/ops.h:24-36) and are normalised on the
+ * fly, C = acc + bias + (resid - mean_r) * rstd_r * ln_w + ln_b, with
+ * ln_stats[2r], ln_stats[2r+1] = (mean_r, rstd_r) of row r as written by
+ * w2v_layer_norm_stats.  resid may alias C.  C, resid, bias, ln_w, ln_b and
+ * ln_stats 16-byte aligned, ldc and ldr multiples of 4. */
+int w2v_gemm_f16_ln_resid(const void* A, long long a_cin, int a_taps, int a_stride, long long a_row_stride,
+                          long long a_rows_in, long long a_batches, long long a_batch_stride, const void* B,
+                          int N, void* C, long long ldc, long long c_batch_rows, int m_valid, const float* bias,
+                          const float* resid, long long ldr, const float* ln_stats, const float* ln_w,
+                          const float* ln_b, int block_n, int* err, void* stream);
 
 /* Failure-detection self-test: launches a kernel whose bounded mbarrier wait
  * (the same wait the GEMM pipeline uses) is never satisfied; after limit_ms
@@ -114,6 +127,14 @@ int w2v_layer_norm(const void* in, int in_f16, long long ld_in, long long in_bat
                    const int* rows, const long long* out_off, int n_batch, int n_rows, int D,
                    const float* w, const float* b, int gelu, float* out32, void* out16,
                    long long ld_out, void* stream);
+
+/* Row LayerNorm (eps 1e-5) of fp32 rows [M, D] -> fp16 rows [M, D], also
+ * writing each row's (mean, 1/sqrt(var + eps)) to stats[2r], stats[2r+1] so
+ * a consumer can re-derive the fp32 normalised row (w2v_gemm_f16_ln_resid)
+ * without it being stored.  D a multiple of 128 (<= 2048); pointers 16-byte
+ * aligned. */
+int w2v_layer_norm_stats(const float* in, long long M, int D, const float* w, const float* b, void* out16,
+                         float* stats, void* stream);
 
 /* Positional conv embedding (src/wav2vec2.cpp:349-356): grouped conv1d over
  * time (kernel Kp, padding Kp/2, G groups, first T of T+1 outputs), GELU,

@@ -132,6 +132,41 @@ def test_gemm_ragged_columns(K, epi, bn):
     assert torch.isnan(out[:, N:]).all()
 
 
+@pytest.mark.parametrize("M,N,Kd,bn", [(700, 768, 768, 0), (4100, 768, 3072, 0), (300, 1024, 1024, -256),
+                                        (257, 1280, 5120, 192)])
+def test_layer_norm_stats_and_ln_resid_gemm(K, M, N, Kd, bn):
+    """Deferred LayerNorm of the post-LN encoder: w2v_layer_norm_stats writes
+    LN(y) in fp16 plus per-row (mean, rstd); w2v_gemm_f16_ln_resid adds the
+    fp32 LN(y) re-derived from y and those statistics to A.W^T + bias, in
+    place over y (src/wav2vec2.cpp:360-373)."""
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    y = torch.randn(M, N, device="cuda", generator=g) * 3 + 0.7
+    lw = 1 + torch.randn(N, device="cuda", generator=g) * 0.1
+    lb = torch.randn(N, device="cuda", generator=g) * 0.1
+    A = torch.randn(M, Kd, device="cuda", generator=g).half()
+    W = (torch.randn(N, Kd, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(N, device="cuda", generator=g)
+    xh = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    stats = torch.empty(M, 2, device="cuda")
+    K.layer_norm_stats(y.data_ptr(), M, N, lw.data_ptr(), lb.data_ptr(), xh.data_ptr(), stats.data_ptr(), stream())
+    torch.cuda.synchronize()
+    yd = y.double()
+    ln = (yd - yd.mean(1, keepdim=True)) / torch.sqrt(yd.var(1, unbiased=False, keepdim=True) + 1e-5) * lw.double() \
+        + lb.double()
+    assert (xh.double() - ln).abs().max().item() < 2e-3 * (1 + ln.abs().max().item())
+    assert (stats[:, 0].double() - yd.mean(1)).abs().max().item() < 1e-5 * (1 + yd.abs().max().item())
+    err = err_word()
+    c = y.clone()
+    K.gemm_ln_resid(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, c.data_ptr(), N, M, M,
+                    bias.data_ptr(), c.data_ptr(), N, stats.data_ptr(), lw.data_ptr(), lb.data_ptr(), bn,
+                    err.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = A.double() @ W.double().T + bias.double() + ln
+    d = (c.double() - ref).abs()
+    assert (d <= 1e-4 * (1 + ref.abs())).all(), d.max().item()
+
+
 @pytest.mark.parametrize("B,C,Lin,k,s,bn", [(3, 512, 1001, 3, 2, -256), (2, 512, 8000, 2, 2, -256),
                                             (4, 128, 600, 3, 2, -128)])
 def test_gemm_cta_pair_conv_view(K, B, C, Lin, k, s, bn):

@@ -59,6 +59,9 @@ SIGNATURES = {
     # kernel layer (include/w2v_kernels.h)
     "w2v_gemm_f16": (_i, [_vp, _ll, _i, _i, _ll, _ll, _ll, _ll, _vp, _i, _vp, _ll, _ll, _i, _vp, _vp, _ll, _i,
                           _i, _vp, _vp]),
+    "w2v_gemm_f16_ln_resid": (_i, [_vp, _ll, _i, _i, _ll, _ll, _ll, _ll, _vp, _i, _vp, _ll, _ll, _i, _vp, _vp,
+                                   _ll, _vp, _vp, _vp, _i, _vp, _vp]),
+    "w2v_layer_norm_stats": (_i, [_vp, _ll, _i, _vp, _vp, _vp, _vp, _vp]),
     "w2v_selftest_wait_timeout": (_i, [_vp, _i, _vp]),
     "w2v_dequant_f16": (_i, [_vp, _i, _ll, _ll, _vp, _vp]),
     "w2v_wave_stats": (_i, [_vp, _vp, _vp, _i, _vp, _vp]),
@@ -254,6 +257,20 @@ class kernels:
                                          a_batch_stride, B, N, Cp, ldc, c_batch_rows, m_valid, bias or None,
                                          resid or None, ldr, epilogue, block_n, err or None, stream or None),
                       "w2v_gemm_f16")
+
+    @staticmethod
+    def gemm_ln_resid(A, a_cin, a_taps, a_stride, a_row_stride, a_rows_in, a_batches, a_batch_stride, B, N, Cp,
+                      ldc, c_batch_rows, m_valid, bias, resid, ldr, ln_stats, ln_w, ln_b, block_n=0, err=0,
+                      stream=0):
+        kernels.check(lib().w2v_gemm_f16_ln_resid(A, a_cin, a_taps, a_stride, a_row_stride, a_rows_in, a_batches,
+                                                  a_batch_stride, B, N, Cp, ldc, c_batch_rows, m_valid,
+                                                  bias or None, resid, ldr, ln_stats, ln_w, ln_b, block_n,
+                                                  err or None, stream or None), "w2v_gemm_f16_ln_resid")
+
+    @staticmethod
+    def layer_norm_stats(inp, M, D, w, b, out16, stats, stream=0):
+        kernels.check(lib().w2v_layer_norm_stats(inp, M, D, w, b, out16, stats, stream or None),
+                      "w2v_layer_norm_stats")
 
     @staticmethod
     def dequant(raw, gtype, n_rows, K, out, stream=0):

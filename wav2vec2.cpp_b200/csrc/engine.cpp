@@ -188,7 +188,7 @@ Engine::~Engine() {
     auto rel = [](DevBuf& b) { b.release(); };
     for (DevBuf* b : {&conv0_w_, &conv0_b_, &proj_lnw_, &proj_lnb_, &proj_w_, &proj_b_, &pos_w_, &pos_b_, &enc_lnw_,
                       &enc_lnb_, &lm_w_, &lm_b_, &audio_stage_, &meta_, &stats_, &gn_, &actA_, &actB_, &feat_,
-                      &pbuf_, &x_, &xh_, &qkv_, &attn_, &hbuf_, &ybuf_, &logits_, &ids_, &spans_, &nspans_, &err_})
+                      &pbuf_, &x_, &xh_, &qkv_, &attn_, &hbuf_, &ybuf_, &lnstats_, &logits_, &ids_, &spans_, &nspans_, &err_})
         rel(*b);
     for (auto* v : {&conv_w_, &conv_b_, &conv_gw_, &conv_gb_})
         for (auto& b : *v) rel(b);
@@ -389,6 +389,7 @@ void Engine::ensure_workspace(const BatchGeom& g) {
     pbuf_.ensure(M * H * 4);
     x_.ensure(M * H * 4);
     ybuf_.ensure(M * H * 4);
+    lnstats_.ensure(M * 2 * sizeof(float));
     xh_.ensure(M * H * 2);
     attn_.ensure(M * H * 2);
     qkv_.ensure(M * 3 * H * 2);
@@ -562,19 +563,46 @@ void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, fl
                [&] { return w2v_attention(qkv_.p, attn_.p, d_T_off_, d_T_, B, H, n_heads, g.T_max, M, err, st); });
     };
     if (!c.stable) {
-        // post-LN encoder (src/wav2vec2.cpp:360-373)
-        ln_rows(x, x, xh_.p, enc_lnw_, enc_lnb_);
-        dbg_copy(1, x);
+        // post-LN encoder (src/wav2vec2.cpp:360-373).  x holds the raw
+        // (pre-LayerNorm) residual stream and is updated in place: each
+        // LayerNorm writes only its fp16 rows (the next GEMM's input) and the
+        // rows' (mean, rstd); the next residual GEMM re-derives the fp32
+        // normalised rows from x and those statistics in its epilogue, so the
+        // normalised stream is never stored.
+        float* lst = lnstats_.as<float>();
+        auto ln_stats = [&](const DevBuf& w, const DevBuf& b) {
+            launch(P_LN, 0.0, st, "layer_norm", [&] {
+                return w2v_layer_norm_stats(x, M, H, w.as<float>(), b.as<float>(), xh_.p, lst, st);
+            });
+        };
+        auto resid_ln_gemm = [&](const void* A, int K, const DevBuf& W, const DevBuf& bias, const DevBuf& lw,
+                                 const DevBuf& lb) {
+            launch(P_GEMM_ENC, 2.0 * M * H * K, st, "gemm", [&] {
+                return w2v_gemm_f16_ln_resid(A, K, 1, 1, K, M, 1, M * K, W.p, H, x, H, M, (int)M,
+                                             bias.as<float>(), x, H, lst, lw.as<float>(), lb.as<float>(), 0, err, st);
+            });
+        };
+        auto dbg_norm = [&](int block, const DevBuf& lw, const DevBuf& lb) {   // debug: materialise LN(x)
+            if (!dbg_stages) return;
+            ln_rows(x, ybuf_.as<float>(), nullptr, lw, lb);
+            dbg_copy(block, ybuf_.as<float>());
+        };
+        ln_stats(enc_lnw_, enc_lnb_);
+        dbg_norm(1, enc_lnw_, enc_lnb_);
+        const DevBuf* pw = &enc_lnw_;   // the LayerNorm that x currently stands for
+        const DevBuf* pb = &enc_lnb_;
         for (int l = 0; l < c.n_layers; l++) {
             const auto& L = layers_[l];
             plain_gemm(P_GEMM_ENC, xh_.p, H, L.wqkv.p, 3 * H, qkv_.p, L.bqkv.p, nullptr, W2V_EPI_F16);
             attention();
-            plain_gemm(P_GEMM_ENC, attn_.p, H, L.wo.p, H, ybuf_.p, L.bo.p, x, W2V_EPI_F32_RESID);
-            ln_rows(ybuf_.as<float>(), x, xh_.p, L.ln1w, L.ln1b);
+            resid_ln_gemm(attn_.p, H, L.wo, L.bo, *pw, *pb);
+            ln_stats(L.ln1w, L.ln1b);
             plain_gemm(P_GEMM_ENC, xh_.p, H, L.w1.p, F, hbuf_.p, L.b1.p, nullptr, W2V_EPI_F16_GELU);
-            plain_gemm(P_GEMM_ENC, hbuf_.p, F, L.w2.p, H, ybuf_.p, L.b2.p, x, W2V_EPI_F32_RESID);
-            ln_rows(ybuf_.as<float>(), x, xh_.p, L.ln2w, L.ln2b);
-            dbg_copy(2 + l, x);
+            resid_ln_gemm(hbuf_.p, F, L.w2, L.b2, L.ln1w, L.ln1b);
+            ln_stats(L.ln2w, L.ln2b);
+            pw = &L.ln2w;
+            pb = &L.ln2b;
+            dbg_norm(2 + l, L.ln2w, L.ln2b);
         }
     } else {
         // pre-LN ("stable layer norm") encoder (src/wav2vec2.cpp:374-392)

@@ -139,6 +139,7 @@ private:
     DevBuf stats_, gn_;
     DevBuf actA_, actB_;                       // fp16 conv ping-pong
     DevBuf feat_, pbuf_, x_, xh_, qkv_, attn_, hbuf_, ybuf_;
+    DevBuf lnstats_;                           // per encoder row (mean, rstd) of the latest LayerNorm
     DevBuf logits_, ids_, spans_, nspans_;
     DevBuf err_;
     long long last_M_ = 0;

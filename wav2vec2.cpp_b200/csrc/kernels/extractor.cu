@@ -631,7 +631,7 @@ __global__ void __launch_bounds__(256)
 layer_norm_vec_kernel(const void* __restrict__ in, int in_f16, long long ld_in, long long in_batch_rows,
                       const int* __restrict__ rows, const long long* __restrict__ out_off, int n_batch, int n_rows,
                       const float* __restrict__ w, const float* __restrict__ b, int gelu, float* __restrict__ out32,
-                      __half* __restrict__ out16, long long ld_out) {
+                      __half* __restrict__ out16, long long ld_out, float2* __restrict__ stats) {
     constexpr int D = 128 * NV;
     const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -668,6 +668,7 @@ layer_norm_vec_kernel(const void* __restrict__ in, int in_f16, long long ld_in, 
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
     const float inv = 1.f / sqrtf(q / D + 1e-5f);
+    if (stats && lane == 0) stats[orow] = make_float2(mean, inv);
 #pragma unroll
     for (int i = 0; i < NV; i++) {
         const int col = 4 * (lane + 32 * i);
@@ -867,7 +868,7 @@ extern "C" int w2v_layer_norm(const void* in, int in_f16, long long ld_in, long 
     case NV:                                                                                                    \
         layer_norm_vec_kernel<NV><<<grid, warps * 32, 0, S(stream)>>>(in, in_f16, ld_in, in_batch_rows, rows,    \
                                                                       out_off, nb, n_rows, w, b, gelu, out32,   \
-                                                                      (__half*)out16, ld_out);                  \
+                                                                      (__half*)out16, ld_out, nullptr);         \
         return launch_rc();
     if (vec_ok) {
         switch (D / 128) {
@@ -886,6 +887,30 @@ extern "C" int w2v_layer_norm(const void* in, int in_f16, long long ld_in, long 
                                                                   nb, n_rows, D, w, b, gelu, out32,
                                                                   (__half*)out16, ld_out);
     return launch_rc();
+}
+
+extern "C" int w2v_layer_norm_stats(const float* in, long long M, int D, const float* w, const float* b,
+                                    void* out16, float* stats, void* stream) {
+    if (D % 128 || D > 16 * 128 || D <= 0 || M < 0 || !in || !w || !b || !out16 || !stats) return W2V_ERR_ARGS;
+    const uintptr_t align = reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(w) |
+                            reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(out16) |
+                            reinterpret_cast<uintptr_t>(stats);
+    if (align % 16) return W2V_ERR_ARGS;
+    if (M == 0) return W2V_OK;
+    const int warps = 8;
+    const unsigned grid = (unsigned)((M + warps - 1) / warps);
+    float2* st2 = reinterpret_cast<float2*>(stats);
+#define W2V_LN_ST(NV)                                                                                           \
+    case NV:                                                                                                    \
+        layer_norm_vec_kernel<NV><<<grid, warps * 32, 0, S(stream)>>>(in, 0, D, M, nullptr, nullptr, 1, (int)M,  \
+                                                                      w, b, 0, nullptr, (__half*)out16, D, st2); \
+        return launch_rc();
+    switch (D / 128) {
+        W2V_LN_ST(1) W2V_LN_ST(2) W2V_LN_ST(3) W2V_LN_ST(4) W2V_LN_ST(5) W2V_LN_ST(6) W2V_LN_ST(8)
+        W2V_LN_ST(10) W2V_LN_ST(12) W2V_LN_ST(16)
+        default: return W2V_ERR_ARGS;
+    }
+#undef W2V_LN_ST
 }
 
 extern "C" int w2v_ctc_greedy(const float* logits, const long long* off, const int* T, int n_utt, int V, int* ids,

@@ -51,6 +51,9 @@ struct GemmParams {
     const float* resid;
     long long ldr;
     int* err;
+    const float2* ln_stats;   // W2V_EPI_F32_RESID_LN: per resid row (mean, rstd)
+    const float* ln_w;
+    const float* ln_b;
 };
 
 template <int BN>
@@ -139,6 +142,7 @@ W2V_DEV void epilogue_chunk(const GemmParams& p, long long out_row, long long re
 
 // Residual of this thread's 8 (row, 4-column) cells of a chunk; rows past
 // m_valid and columns past N read as zero.
+template <int EPI>
 W2V_DEV void load_resid_t(const GemmParams& p, long long out_row0, int row0, int col0, float4 (&res)[8]) {
     const int lane = threadIdx.x & 31, cg = lane & 7, rs = lane >> 3;
     const int col = col0 + 4 * cg;
@@ -158,13 +162,35 @@ W2V_DEV void load_resid_t(const GemmParams& p, long long out_row0, int row0, int
     }
 }
 
+// W2V_EPI_F32_RESID_LN: the (mean, rstd) of this thread's 8 rows of the tile
+// (rows t/8 + 4i of the warp's 32), fetched once per tile.
+W2V_DEV void load_ln_stats_t(const GemmParams& p, long long out_row0, int row0, float2 (&st)[8]) {
+    const int rs = (threadIdx.x & 31) >> 3;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int r = rs + 4 * i;
+        st[i] = row0 + r < p.m_valid ? p.ln_stats[out_row0 + r] : make_float2(0.f, 0.f);
+    }
+}
+
 template <int EPI>
 W2V_DEV void epilogue_chunk_t(const GemmParams& p, const float* stg, long long out_row0, int row0, int col0,
-                              const float4 (&res)[8]) {
+                              const float4 (&res)[8], const float2 (&st)[8]) {
     const int lane = threadIdx.x & 31, cg = lane & 7, rs = lane >> 3;
     const int col = col0 + 4 * cg;
     if (col >= p.N) return;
     const bool full4 = col + 3 < p.N;
+    float4 lw = make_float4(0.f, 0.f, 0.f, 0.f), lb = lw;
+    if (EPI == W2V_EPI_F32_RESID_LN) {
+        if (full4) {
+            lw = __ldg(reinterpret_cast<const float4*>(p.ln_w + col));
+            lb = __ldg(reinterpret_cast<const float4*>(p.ln_b + col));
+        } else {
+            lw.x = __ldg(p.ln_w + col); lb.x = __ldg(p.ln_b + col);
+            if (col + 1 < p.N) { lw.y = __ldg(p.ln_w + col + 1); lb.y = __ldg(p.ln_b + col + 1); }
+            if (col + 2 < p.N) { lw.z = __ldg(p.ln_w + col + 2); lb.z = __ldg(p.ln_b + col + 2); }
+        }
+    }
     float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
     if (p.bias) {
         if (full4) b = __ldg(reinterpret_cast<const float4*>(p.bias + col));
@@ -188,6 +214,13 @@ W2V_DEV void epilogue_chunk_t(const GemmParams& p, const float* stg, long long o
         }
         if (EPI == W2V_EPI_F32_RESID) {
             x.x += res[i].x; x.y += res[i].y; x.z += res[i].z; x.w += res[i].w;
+        }
+        if (EPI == W2V_EPI_F32_RESID_LN) {
+            // the LayerNorm this raw residual row stands for (same expression as the row LayerNorm kernel)
+            x.x += (res[i].x - st[i].x) * st[i].y * lw.x + lb.x;
+            x.y += (res[i].y - st[i].x) * st[i].y * lw.y + lb.y;
+            x.z += (res[i].z - st[i].x) * st[i].y * lw.z + lb.z;
+            x.w += (res[i].w - st[i].x) * st[i].y * lw.w + lb.w;
         }
     }
 #pragma unroll
@@ -224,7 +257,7 @@ W2V_DEV void epilogue_chunk_t(const GemmParams& p, const float* stg, long long o
 // row0 .. row0+31 of the batch), 32-column chunks c0 .. c1-1.
 template <int EPI>
 W2V_DEV void epilogue_warp(const GemmParams& p, uint32_t tmem_row, float* stg, long long out_row0, int row0,
-                           int col_base, int c0, int c1, float4 (&res)[8]) {
+                           int col_base, int c0, int c1, float4 (&res)[8], const float2 (&st)[8]) {
     const int lane = threadIdx.x & 31;
     if (!p.vec) {
         // unaligned C or residual: row-per-thread scalar path
@@ -247,11 +280,12 @@ W2V_DEV void epilogue_warp(const GemmParams& p, uint32_t tmem_row, float* stg, l
 #pragma unroll
         for (int i = 0; i < 8; i++) cur[i] = res[i];
         // next chunk's residual loads are in flight while this chunk is stored
-        if (EPI == W2V_EPI_F32_RESID && c + 1 < c1 && col0 + 32 < p.N) load_resid_t(p, out_row0, row0, col0 + 32, res);
+        if ((EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) && c + 1 < c1 && col0 + 32 < p.N)
+            load_resid_t<EPI>(p, out_row0, row0, col0 + 32, res);
         __syncwarp();
         stage_put(stg, v);
         __syncwarp();
-        epilogue_chunk_t<EPI>(p, stg, out_row0, row0, col0, cur);
+        epilogue_chunk_t<EPI>(p, stg, out_row0, row0, col0, cur, st);
     }
     __syncwarp();
 }
@@ -361,13 +395,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const long long out_row0 = (long long)b * p.c_batch_rows + row0;
             const int c0 = half * kChunks;
             float4 res[8];
+            float2 lst[8];
             // the residual does not depend on the MMA: fetch it while the MMA runs
-            if (EPI == W2V_EPI_F32_RESID && p.vec && ni * BN + c0 * 32 < p.N)
-                load_resid_t(p, out_row0, row0, ni * BN + c0 * 32, res);
+            if ((EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) && p.vec && ni * BN + c0 * 32 < p.N)
+                load_resid_t<EPI>(p, out_row0, row0, ni * BN + c0 * 32, res);
+            if (EPI == W2V_EPI_F32_RESID_LN) load_ln_stats_t(p, out_row0, row0, lst);
             if (!mbar_wait(&tfull[ab], aph, p.err)) break;
             tc_fence_after();
             epilogue_warp<EPI>(p, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN), stg, out_row0, row0,
-                               ni * BN, c0, c0 + kChunks, res);
+                               ni * BN, c0, c0 + kChunks, res, lst);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[ab]);
@@ -533,12 +569,14 @@ gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             const long long out_row0 = (long long)b * p.c_batch_rows + row0;
             const int c0 = half * kChunks;
             float4 res[8];
-            if (EPI == W2V_EPI_F32_RESID && p.vec && ni * BN + c0 * 32 < p.N)
-                load_resid_t(p, out_row0, row0, ni * BN + c0 * 32, res);
+            float2 lst[8];
+            if ((EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) && p.vec && ni * BN + c0 * 32 < p.N)
+                load_resid_t<EPI>(p, out_row0, row0, ni * BN + c0 * 32, res);
+            if (EPI == W2V_EPI_F32_RESID_LN) load_ln_stats_t(p, out_row0, row0, lst);
             if (!mbar_wait(&tfull[ab], aph, p.err)) break;
             tc_fence_after();
             epilogue_warp<EPI>(p, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN), stg, out_row0, row0,
-                               ni * BN, c0, c0 + kChunks, res);
+                               ni * BN, c0, c0 + kChunks, res, lst);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_lead + (uint32_t)(ab * 8));
@@ -686,7 +724,7 @@ static int pick_bn(int N, int m_valid, int n_batch, long long K, int epilogue) {
     const long long mt1 = (long long)((m_valid + kBM - 1) / kBM) * n_batch;
     const long long mt2 = (long long)((m_valid + 2 * kBM - 1) / (2 * kBM)) * n_batch;
     const double E = epilogue == W2V_EPI_F16 ? 293 : epilogue == W2V_EPI_F16_GELU ? 442
-                   : epilogue == W2V_EPI_F32 ? 450 : 932;
+                   : epilogue == W2V_EPI_F32 ? 450 : epilogue == W2V_EPI_F32_RESID ? 932 : 1000;
     int best = 64;
     double best_cost = 1e300;
     for (int bn : {256, 192, 128, 64, -256, -192, -128}) {
@@ -715,11 +753,11 @@ extern "C" int w2v_selftest_wait_timeout(int* err, int limit_ms, void* stream) {
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
-extern "C" int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_stride, long long a_row_stride,
-                            long long a_rows_in, long long a_batches, long long a_batch_stride, const void* B,
-                            int N, void* C, long long ldc, long long c_batch_rows, int m_valid, const float* bias,
-                            const float* resid, long long ldr, int epilogue, int block_n, int* err,
-                            void* stream) {
+static int gemm_impl(const void* A, long long a_cin, int a_taps, int a_stride, long long a_row_stride,
+                     long long a_rows_in, long long a_batches, long long a_batch_stride, const void* B, int N,
+                     void* C, long long ldc, long long c_batch_rows, int m_valid, const float* bias,
+                     const float* resid, long long ldr, int epilogue, const float* ln_stats, const float* ln_w,
+                     const float* ln_b, int block_n, int* err, void* stream) {
     if (a_cin % kBK != 0 || a_cin <= 0 || a_taps <= 0 || a_stride <= 0 || N <= 0 || a_rows_in <= 0 ||
         a_batches <= 0 || m_valid < 0 || a_row_stride < a_cin)
         return W2V_ERR_ARGS;
@@ -760,6 +798,9 @@ extern "C" int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_st
     p.resid = resid;
     p.ldr = ldr;
     p.err = err;
+    p.ln_stats = reinterpret_cast<const float2*>(ln_stats);
+    p.ln_w = ln_w;
+    p.ln_b = ln_b;
     {
         const bool f16 = epilogue == W2V_EPI_F16 || epilogue == W2V_EPI_F16_GELU;
         const uintptr_t cb = reinterpret_cast<uintptr_t>(C), rb = reinterpret_cast<uintptr_t>(resid),
@@ -780,6 +821,34 @@ extern "C" int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_st
         case W2V_EPI_F32_RESID:
             if (!resid) return W2V_ERR_ARGS;
             return launch_epi<W2V_EPI_F32_RESID>(bn, ta, tb, p, st);
+        case W2V_EPI_F32_RESID_LN:
+            if (!resid || !ln_stats || !ln_w || !ln_b || !p.vec ||
+                ((reinterpret_cast<uintptr_t>(ln_stats) | reinterpret_cast<uintptr_t>(ln_w) |
+                  reinterpret_cast<uintptr_t>(ln_b)) & 15))
+                return W2V_ERR_ARGS;
+            return launch_epi<W2V_EPI_F32_RESID_LN>(bn, ta, tb, p, st);
         default: return W2V_ERR_ARGS;
     }
+}
+
+extern "C" int w2v_gemm_f16(const void* A, long long a_cin, int a_taps, int a_stride, long long a_row_stride,
+                            long long a_rows_in, long long a_batches, long long a_batch_stride, const void* B,
+                            int N, void* C, long long ldc, long long c_batch_rows, int m_valid, const float* bias,
+                            const float* resid, long long ldr, int epilogue, int block_n, int* err,
+                            void* stream) {
+    if (epilogue == W2V_EPI_F32_RESID_LN) return W2V_ERR_ARGS;   // needs the statistics: w2v_gemm_f16_ln_resid
+    return gemm_impl(A, a_cin, a_taps, a_stride, a_row_stride, a_rows_in, a_batches, a_batch_stride, B, N, C, ldc,
+                     c_batch_rows, m_valid, bias, resid, ldr, epilogue, nullptr, nullptr, nullptr, block_n, err,
+                     stream);
+}
+
+extern "C" int w2v_gemm_f16_ln_resid(const void* A, long long a_cin, int a_taps, int a_stride,
+                                     long long a_row_stride, long long a_rows_in, long long a_batches,
+                                     long long a_batch_stride, const void* B, int N, void* C, long long ldc,
+                                     long long c_batch_rows, int m_valid, const float* bias, const float* resid,
+                                     long long ldr, const float* ln_stats, const float* ln_w, const float* ln_b,
+                                     int block_n, int* err, void* stream) {
+    return gemm_impl(A, a_cin, a_taps, a_stride, a_row_stride, a_rows_in, a_batches, a_batch_stride, B, N, C, ldc,
+                     c_batch_rows, m_valid, bias, resid, ldr, W2V_EPI_F32_RESID_LN, ln_stats, ln_w, ln_b, block_n,
+                     err, stream);
 }
