@@ -294,28 +294,31 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
         if (elect_one()) {
             constexpr uint32_t idesc_s = umma_idesc_f16(128, KV);
             constexpr uint32_t idesc_o = umma_idesc_f16_bmn(128, D);
+            // descriptors built once, advanced by (byte offset >> 4) in their
+            // start-address field (shared memory < 256 KB: no carry out of it)
+            const uint64_t q_desc = umma_desc_sw128(smem_u32(sQ));
+            const uint64_t k_desc0 = umma_desc_sw128(smem_u32(sKV));
+            const uint64_t v_desc0 = umma_desc_sw128_mn(smem_u32(sKV + Cfg::kTileKV), Cfg::kAtomKV);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = mbar_wait(q_full, 0, err);
             for (int j = 0; j < n_kv && ok; j++) {
                 if (!mbar_wait(&kv_full[stage], phase, err)) break;
                 tc_fence_after();
-                const uint32_t q_addr = smem_u32(sQ);
-                const uint32_t k_addr = smem_u32(sKV + stage * 2 * Cfg::kTileKV);
-                const uint32_t v_addr = k_addr + Cfg::kTileKV;
+                const uint64_t so = (uint64_t)((stage * 2 * Cfg::kTileKV) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++) {
                     const uint32_t oq = (kk / 4) * Cfg::kAtomQ + (kk % 4) * 32;
                     const uint32_t ok_ = (kk / 4) * Cfg::kAtomKV + (kk % 4) * 32;
-                    umma_f16(tS, umma_desc_sw128(q_addr + oq), umma_desc_sw128(k_addr + ok_), idesc_s, kk > 0);
+                    umma_f16(tS, q_desc + (oq >> 4), k_desc0 + so + (ok_ >> 4), idesc_s, kk > 0);
                 }
                 umma_commit(s_full);
                 if (!mbar_wait(p_full, (uint32_t)j & 1u, err)) break;
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < KV / 16; kk++)
-                    umma_f16_tmem_a(tO, tS + (uint32_t)(kk * 8), umma_desc_sw128_mn(v_addr + kk * 2048, Cfg::kAtomKV),
-                                    idesc_o, (j > 0 || kk > 0));
+                    umma_f16_tmem_a(tO, tS + (uint32_t)(kk * 8), v_desc0 + so + (uint64_t)(kk * 2048 >> 4), idesc_o,
+                                    (j > 0 || kk > 0));
                 umma_commit(&kv_empty[stage]);
                 if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
             }

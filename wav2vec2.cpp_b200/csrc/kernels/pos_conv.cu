@@ -104,28 +104,32 @@ __global__ void __launch_bounds__(192, 1) pos_conv_tc_kernel(PosConvArgs a) {
     } else if (warp == 1) {
         if (elect_one()) {
             constexpr uint32_t idesc = umma_idesc_f16(128, CG);
+            // Descriptors are built once and advanced by adding (byte offset >> 4)
+            // to their start-address field (shared memory < 256 KB: no carry out of
+            // the field), keeping the single issuing thread's work per MMA to an add.
+            const uint64_t a_desc0 = umma_desc_noswz(smem_u32(sA), Cfg::kChunkA, 128);
+            const uint64_t b_desc0 = umma_desc_noswz(smem_u32(sB), Cfg::kChunkB, 128);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = mbar_wait(a_ready, 0, a.err);
             for (int i = 0; i < n_stages_total && ok; i++) {
                 if (!mbar_wait(&full[stage], phase, a.err)) break;
                 tc_fence_after();
-                const uint32_t b_stage = smem_u32(sB + stage * Cfg::kStageBytes);
-                const uint32_t a0 = smem_u32(sA);
+                const uint64_t b_stage = b_desc0 + (uint64_t)((stage * Cfg::kStageBytes) >> 4);
+#pragma unroll
                 for (int tt = 0; tt < kPcTaps; tt++) {
                     const int k = i * kPcTaps + tt;
+                    const uint64_t a_tap = a_desc0 + (uint64_t)k;      // k rows of 16 bytes
 #pragma unroll
                     for (int s = 0; s < CG / 16; s++) {
-                        const uint64_t bd = umma_desc_noswz(b_stage + tt * Cfg::kTapBytes + 2 * s * Cfg::kChunkB,
-                                                            Cfg::kChunkB, 128);
+                        const uint64_t bd = b_stage + (uint64_t)((tt * Cfg::kTapBytes + 2 * s * Cfg::kChunkB) >> 4);
+                        const uint32_t acc = (k | s) != 0;
 #pragma unroll
-                        for (int r = 0; r < kPcTiles; r++) {
-                            if (r < n_tiles) {
-                                const uint64_t ad =
-                                    umma_desc_noswz(a0 + 2 * s * Cfg::kChunkA + (r * 128 + k) * 16, Cfg::kChunkA, 128);
-                                umma_f16(tmem_base + (uint32_t)(r * CG), ad, bd, idesc, (k | s) != 0);
-                            }
-                        }
+                        for (int r = 0; r < kPcTiles; r++)
+                            if (r < n_tiles)
+                                umma_f16(tmem_base + (uint32_t)(r * CG),
+                                         a_tap + (uint64_t)((2 * s * Cfg::kChunkA + r * 128 * 16) >> 4), bd, idesc,
+                                         acc);
                     }
                 }
                 umma_commit(&empty[stage]);
@@ -138,19 +142,35 @@ __global__ void __launch_bounds__(192, 1) pos_conv_tc_kernel(PosConvArgs a) {
         // stage the input window: row w is frame t0 - Kp/2 + w, zero outside [0, T)
         const int et = threadIdx.x - 64;                       // 0..127
         const int rows = kPcFrames + Kp;
-        for (int i = et; i < rows * Cfg::kChunks; i += 128) {
-            const int w = i % rows, c = i / rows;
-            const int t = t0 - half + w;
-            uint4 p = make_uint4(0, 0, 0, 0);
-            if (t >= 0 && t < T) {
-                const float4* src = reinterpret_cast<const float4*>(a.xin + (base + t) * a.H + g * CG + c * 8);
-                const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
-                p.x = pack_half2(v0.x, v0.y);
-                p.y = pack_half2(v0.z, v0.w);
-                p.z = pack_half2(v1.x, v1.y);
-                p.w = pack_half2(v1.z, v1.w);
+        const int n_items = rows * Cfg::kChunks;
+        constexpr int kBatch = 6;                              // loads in flight per thread
+        for (int i0 = et; i0 < n_items; i0 += 128 * kBatch) {
+            float4 v[kBatch][2];
+#pragma unroll
+            for (int j = 0; j < kBatch; j++) {
+                const int i = i0 + j * 128;
+                const int w = i % rows, c = i / rows;
+                const int t = t0 - half + w;
+                v[j][0] = v[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (i < n_items && t >= 0 && t < T) {
+                    const float4* src = reinterpret_cast<const float4*>(a.xin + (base + t) * a.H + g * CG + c * 8);
+                    v[j][0] = __ldg(src);
+                    v[j][1] = __ldg(src + 1);
+                }
             }
-            *reinterpret_cast<uint4*>(sA + c * Cfg::kChunkA + w * 16) = p;
+#pragma unroll
+            for (int j = 0; j < kBatch; j++) {
+                const int i = i0 + j * 128;
+                if (i < n_items) {
+                    const int w = i % rows, c = i / rows;
+                    uint4 p;
+                    p.x = pack_half2(v[j][0].x, v[j][0].y);
+                    p.y = pack_half2(v[j][0].z, v[j][0].w);
+                    p.z = pack_half2(v[j][1].x, v[j][1].y);
+                    p.w = pack_half2(v[j][1].z, v[j][1].w);
+                    *reinterpret_cast<uint4*>(sA + c * Cfg::kChunkA + w * 16) = p;
+                }
+            }
         }
         fence_async_smem();
         __syncwarp();
