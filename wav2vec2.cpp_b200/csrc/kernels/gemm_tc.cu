@@ -15,11 +15,13 @@
 //   D  fp32 accumulators in TMEM, two buffers so the epilogue of tile i
 //      overlaps the MMAs of tile i+1.
 //
-// Roles (320 threads, one CTA per SM, persistent over output tiles):
+// Roles (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: STAGES-deep smem ring, mbarrier full/empty.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
-//   warps 2..9  epilogue: tcgen05.ld -> bias / GELU / residual -> global;
-//               two warps per TMEM lane quarter, each taking half the columns.
+//   warps 2..   epilogue (8 warps for fp32 / residual outputs, 12 for fp16
+//               ones): tcgen05.ld -> bias / GELU / residual -> global;
+//               two or three warps per TMEM lane quarter, each taking a
+//               contiguous share of the tile's columns.
 // Every mbarrier wait is bounded (common.cuh); on expiry the kernel records
 // an error code and returns.
 #include "common.cuh"
@@ -30,9 +32,17 @@ namespace w2v {
 constexpr int kBM = 128;       // tile rows (UMMA M)
 constexpr int kBK = 64;        // K per stage (128 B of fp16: one swizzle row)
 constexpr int kUmmaK = 16;     // K per tcgen05.mma kind::f16
-constexpr int kEpiWarps = 8;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kStageBytes = kEpiWarps * 32 * 32 * 4;   // epilogue staging, 4 KB per warp
+// Epilogue warps: 12 (three per TMEM lane quarter) for the fp16 epilogues,
+// whose GELU / conversion work per element is the longest; 8 for the fp32
+// residual epilogues, which hold a prefetched residual chunk in registers.
+__host__ __device__ constexpr int epi_warps(int epi) {
+    return (epi == W2V_EPI_F16 || epi == W2V_EPI_F16_GELU) ? 12 : 8;
+}
+__host__ __device__ constexpr int gemm_threads(int epi) { return 64 + 32 * epi_warps(epi); }
+constexpr int kSmemCap = 232448;        // opt-in dynamic shared memory per block on sm_100
+__host__ __device__ constexpr int fit_stages(int want, int stage_bytes, int fixed_bytes) {
+    return (kSmemCap - fixed_bytes) / stage_bytes < want ? (kSmemCap - fixed_bytes) / stage_bytes : want;
+}
 
 struct GemmParams {
     int vec;              // 16-byte vector stores/loads are aligned for this C / resid
@@ -56,11 +66,13 @@ struct GemmParams {
     const float* ln_b;
 };
 
-template <int BN>
+template <int BN, int NE>
 struct GemmCfg {
-    static constexpr int kStages = BN == 256 ? 4 : BN == 192 ? 4 : BN == 128 ? 6 : 8;
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = BN * kBK * 2;
+    static constexpr int kStageBytes = NE * 32 * 32 * 4;   // epilogue staging, 4 KB per warp
+    static constexpr int kStages = fit_stages(BN == 256 ? 4 : BN == 192 ? 4 : BN == 128 ? 6 : 8, kABytes + kBBytes,
+                                              kStageBytes + 1024 + 256);
     // two accumulators; TMEM is allocated in powers of two columns
     static constexpr int kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
     static constexpr int kSmem = kStages * (kABytes + kBBytes) + kStageBytes + 1024 + 256;
@@ -291,9 +303,10 @@ W2V_DEV void epilogue_warp(const GemmParams& p, uint32_t tmem_row, float* stg, l
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(gemm_threads(EPI), 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
-    using Cfg = GemmCfg<BN>;
+    constexpr int NE = epi_warps(EPI);
+    using Cfg = GemmCfg<BN, NE>;
     constexpr int S = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -301,7 +314,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint8_t* sA = smem;
     uint8_t* sB = smem + S * Cfg::kABytes;
     float* stage_buf = reinterpret_cast<float*>(sB + S * Cfg::kBBytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes + kStageBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes + Cfg::kStageBytes);
     uint64_t* full = bars;
     uint64_t* empty = bars + S;
     uint64_t* tfull = bars + 2 * S;
@@ -313,7 +326,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], kEpiWarps); }
+        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], NE); }
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
@@ -381,8 +394,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         __syncwarp();
     } else {
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
-        const int half = (warp - 2) >> 2;       // which half of the tile's columns
-        constexpr int kChunks = BN / 32 / 2;    // 32-column chunks per warp
+        // NE/4 warps per TMEM lane quarter, each taking a contiguous share of the 32-column chunks
+        const int part = (warp - 2) >> 2;
+        constexpr int kNch = BN / 32, kParts = NE / 4;
+        const int cb = part * kNch / kParts, ce = (part + 1) * kNch / kParts;
         float* stg = stage_buf + (warp - 2) * 32 * 32;
         int it = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, it++) {
@@ -393,17 +408,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const uint32_t aph = (uint32_t)(it >> 1) & 1u;
             const int row0 = mi * kBM + q * 32;
             const long long out_row0 = (long long)b * p.c_batch_rows + row0;
-            const int c0 = half * kChunks;
+            const int c0 = cb;
             float4 res[8];
             float2 lst[8];
             // the residual does not depend on the MMA: fetch it while the MMA runs
-            if ((EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) && p.vec && ni * BN + c0 * 32 < p.N)
+            if ((EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) && p.vec && c0 < ce && ni * BN + c0 * 32 < p.N)
                 load_resid_t<EPI>(p, out_row0, row0, ni * BN + c0 * 32, res);
             if (EPI == W2V_EPI_F32_RESID_LN) load_ln_stats_t(p, out_row0, row0, lst);
             if (!mbar_wait(&tfull[ab], aph, p.err)) break;
             tc_fence_after();
             epilogue_warp<EPI>(p, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN), stg, out_row0, row0,
-                               ni * BN, c0, c0 + kChunks, res, lst);
+                               ni * BN, c0, ce, res, lst);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[ab]);
@@ -430,21 +445,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 //             CTAs' TMA loads complete on it (peer through a cluster address)
 //   empty[s]  each CTA: the leader's MMA commit arrives on both
 //   tfull[b]  each CTA: accumulator b of this CTA's rows is ready
-//   tempty[b] leader: 16 epilogue warps (8 per CTA) have drained accumulator b
+//   tempty[b] leader: the epilogue warps of both CTAs have drained accumulator b
 //   done      leader: every MMA the leader issued has completed (teardown)
-template <int BN>
+template <int BN, int NE>
 struct Gemm2Cfg {
     static constexpr int kABytes = kBM * kBK * 2;
     static constexpr int kBBytes = (BN / 2) * kBK * 2;
-    static constexpr int kStages = BN == 256 ? 6 : BN == 192 ? 6 : 8;
+    static constexpr int kStageBytes = NE * 32 * 32 * 4;
+    static constexpr int kStages = fit_stages(BN == 256 ? 6 : BN == 192 ? 6 : 8, kABytes + kBBytes,
+                                              kStageBytes + 1024 + 256);
     static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
     static constexpr int kSmem = kStages * (kABytes + kBBytes) + kStageBytes + 1024 + 256;
 };
 
 template <int BN, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads(EPI), 1)
 gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
-    using Cfg = Gemm2Cfg<BN>;
+    constexpr int NE = epi_warps(EPI);
+    using Cfg = Gemm2Cfg<BN, NE>;
     constexpr int S = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -454,7 +472,7 @@ gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     uint8_t* sA = smem;
     uint8_t* sB = smem + S * Cfg::kABytes;
     float* stage_buf = reinterpret_cast<float*>(sB + S * Cfg::kBBytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes + kStageBytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes + Cfg::kStageBytes);
     uint64_t* full = bars;
     uint64_t* empty = bars + S;
     uint64_t* tfull = bars + 2 * S;
@@ -469,7 +487,7 @@ gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 2 * kEpiWarps); }
+        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], 2 * NE); }
         mbar_init(done, 1);
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
@@ -554,8 +572,9 @@ gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         __syncwarp();
     } else {
         const int q = warp & 3;
-        const int half = (warp - 2) >> 2;
-        constexpr int kChunks = BN / 32 / 2;
+        const int part = (warp - 2) >> 2;
+        constexpr int kNch = BN / 32, kParts = NE / 4;
+        const int cb = part * kNch / kParts, ce = (part + 1) * kNch / kParts;
         const uint32_t tempty_lead = mapa_shared(smem_u32(tempty), 0);
         float* stg = stage_buf + (warp - 2) * 32 * 32;
         int it = 0;
@@ -567,16 +586,16 @@ gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             const uint32_t aph = (uint32_t)(it >> 1) & 1u;
             const int row0 = mi * 2 * kBM + (int)rank * kBM + q * 32;
             const long long out_row0 = (long long)b * p.c_batch_rows + row0;
-            const int c0 = half * kChunks;
+            const int c0 = cb;
             float4 res[8];
             float2 lst[8];
-            if ((EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) && p.vec && ni * BN + c0 * 32 < p.N)
+            if ((EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) && p.vec && c0 < ce && ni * BN + c0 * 32 < p.N)
                 load_resid_t<EPI>(p, out_row0, row0, ni * BN + c0 * 32, res);
             if (EPI == W2V_EPI_F32_RESID_LN) load_ln_stats_t(p, out_row0, row0, lst);
             if (!mbar_wait(&tfull[ab], aph, p.err)) break;
             tc_fence_after();
             epilogue_warp<EPI>(p, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN), stg, out_row0, row0,
-                               ni * BN, c0, c0 + kChunks, res, lst);
+                               ni * BN, c0, ce, res, lst);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_lead + (uint32_t)(ab * 8));
@@ -643,7 +662,7 @@ static int sm_count() {
 
 template <int BN, int EPI>
 static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
-    using Cfg = GemmCfg<BN>;
+    using Cfg = GemmCfg<BN, epi_warps(EPI)>;
     auto kern = gemm_tc_kernel<BN, EPI>;
     static bool attr_set[64] = {};
     int dev = 0;
@@ -655,7 +674,7 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPar
     }
     const int total = p.n_batch * p.m_tiles * p.n_tiles;
     const int grid = total < sm_count() ? total : sm_count();
-    kern<<<grid, kThreads, Cfg::kSmem, st>>>(ta, tb, p);
+    kern<<<grid, gemm_threads(EPI), Cfg::kSmem, st>>>(ta, tb, p);
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
@@ -664,13 +683,13 @@ template <int BN, int EPI>
 static int max_pairs(int dev) {
     static int n[64] = {};
     if (!n[dev & 63]) {
-        using Cfg = Gemm2Cfg<BN>;
+        using Cfg = Gemm2Cfg<BN, epi_warps(EPI)>;
         auto kern = gemm2_tc_kernel<BN, EPI>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) != cudaSuccess)
             return 0;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
-        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.blockDim = dim3(gemm_threads(EPI), 1, 1);
         cfg.dynamicSmemBytes = Cfg::kSmem;
         int c = 0;
         if (cudaOccupancyMaxActiveClusters(&c, kern, &cfg) != cudaSuccess || c <= 0) {
@@ -684,14 +703,14 @@ static int max_pairs(int dev) {
 
 template <int BN, int EPI>
 static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
-    using Cfg = Gemm2Cfg<BN>;
+    using Cfg = Gemm2Cfg<BN, epi_warps(EPI)>;
     int dev = 0;
     cudaGetDevice(&dev);
     const int mp = max_pairs<BN, EPI>(dev);
     if (mp <= 0) return W2V_ERR_LAUNCH;
     const int total = p.n_batch * p.m_tiles * p.n_tiles;
     const int pairs = total < mp ? total : mp;
-    gemm2_tc_kernel<BN, EPI><<<2 * pairs, kThreads, Cfg::kSmem, st>>>(ta, tb, p);
+    gemm2_tc_kernel<BN, EPI><<<2 * pairs, gemm_threads(EPI), Cfg::kSmem, st>>>(ta, tb, p);
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
