@@ -43,6 +43,7 @@ CASES = [
     ("tiny_f16_1s", "tiny", "f16", {"bias_std": 0.02, "gain_jitter": 0.1}, 1.0, 4),
     ("tiny_pre_q4_0_1s", "tiny_pre", "q4_0", {"bias_std": 0.02, "gain_jitter": 0.1}, 1.0, 5),
     ("tiny_q8_0_short", "tiny", "q8_0", {"bias_std": 0.02, "gain_jitter": 0.1}, 0.05, 6),
+    ("tiny80_f16_1s", "tiny80", "f16", {"bias_std": 0.02, "gain_jitter": 0.1}, 1.0, 7),
 ]
 
 

@@ -61,7 +61,7 @@ def test_tiny_logits_vs_oracle(W, model_path, synth, arch, dtype):
 
 
 @pytest.mark.parametrize("case", ["base_q8_0_2s", "base_q4_0_2s", "base_f16_1s", "large_q8_0_1s",
-                                  "tiny_f16_1s", "tiny_pre_q4_0_1s", "base_q8_0_10s"])
+                                  "tiny_f16_1s", "tiny_pre_q4_0_1s", "base_q8_0_10s", "tiny80_f16_1s"])
 def test_logits_vs_reference_golden(W, model_path, synth, case):
     g = load_golden(case)
     m = model(W, golden_model(model_path, g))

@@ -7,10 +7,11 @@
 // unpadded single-utterance computation.
 //
 // fp16 Q/K/V/P operands with fp32 accumulation and fp32 softmax statistics.
-// Two implementations: head dims 64 and 128 run the tcgen05 kernel below
-// (attn_tc_kernel); head dim 80 (XLS-R-1B) runs the warp-level mma.sync
-// kernel (attn_kernel: 64 queries x 64 keys per step, 4 warps x 16 query
-// rows, K/V double buffered with cp.async).
+// The tcgen05 kernel below (attn_tc_kernel) runs every published head dim:
+// 64 and 128 with 128-byte-swizzled tiles, 80 (XLS-R-1B) with no-swizzle
+// core-matrix tiles.  The warp-level mma.sync kernel (attn_kernel: 64 queries
+// x 64 keys per step, K/V double buffered with cp.async) remains only for a
+// qkv buffer that TMA cannot address (not 16-byte aligned).
 #include "common.cuh"
 #include "w2v_kernels.h"
 
@@ -199,9 +200,9 @@ attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, const long
 // TMEM: S/P at columns 0..KV-1, O at KV..KV+D-1.  With KV = 64 and D = 64 a
 // CTA holds 128 columns and 50 KB of shared memory, so four CTAs share an SM
 // and hide each other's handoff latencies.
-template <int D, int KV>
+template <int D, int KV, bool NS = false>
 struct AttnTc {
-    static constexpr int kAtoms = D / 64;               // 64-column swizzle atoms per row
+    static constexpr int kAtoms = NS ? 1 : D / 64;      // 64-column swizzle atoms per row
     static constexpr int kTileQ = 128 * D * 2;
     static constexpr int kTileKV = KV * D * 2;          // one K or V tile
     static constexpr int kAtomQ = 128 * 128;            // 128 rows x 128 B
@@ -215,12 +216,17 @@ struct AttnTc {
 
 constexpr float kLazyRescaleLog2 = 8.f;
 
-template <int D, int KV>
-__global__ void __launch_bounds__(192, AttnTc<D, KV>::kMinBlocks)
+// NS (head dims that are not a multiple of 64, e.g. 80): Q, K and V tiles are
+// loaded through a 3-D view (8 columns, rows, column chunks of 8) into the
+// no-swizzle core-matrix layout [chunk][row][16 bytes]; Q and K are read as
+// K-major operands (LBO = chunk stride, SBO = 8 rows), V as the MN-major
+// operand (SBO = chunk stride, LBO = 8 keys).
+template <int D, int KV, bool NS>
+__global__ void __launch_bounds__(192, AttnTc<D, KV, NS>::kMinBlocks)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
                __half* __restrict__ out, const long long* __restrict__ off, const int* __restrict__ Tn, int H,
                float scale_log2, int* err) {
-    using Cfg = AttnTc<D, KV>;
+    using Cfg = AttnTc<D, KV, NS>;
     constexpr int kChunks = KV / 32;
     const int u = blockIdx.z, h = blockIdx.y;
     const int T = Tn[u];
@@ -265,9 +271,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
     if (warp == 0) {
         if (elect_one()) {
             mbar_arrive_expect_tx(q_full, Cfg::kTileQ);
+            if constexpr (NS) {
+                tma_load_3d(sQ, &tmq, q_full, 0, (int)(base + q0), colQ / 8);
+            } else {
 #pragma unroll
-            for (int a = 0; a < Cfg::kAtoms; a++)
-                tma_load_2d(sQ + a * Cfg::kAtomQ, &tmq, q_full, colQ + 64 * a, (int)(base + q0));
+                for (int a = 0; a < Cfg::kAtoms; a++)
+                    tma_load_2d(sQ + a * Cfg::kAtomQ, &tmq, q_full, colQ + 64 * a, (int)(base + q0));
+            }
             int stage = 0;
             uint32_t phase = 0, issued = 0, last_par = 0;
             for (int j = 0; j < n_kv; j++) {
@@ -275,10 +285,17 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
                 mbar_arrive_expect_tx(&kv_full[stage], 2 * Cfg::kTileKV);
                 uint8_t* sK = sKV + stage * 2 * Cfg::kTileKV;
                 uint8_t* sV = sK + Cfg::kTileKV;
+                if constexpr (NS) {
+                    tma_load_3d(sK, &tmkv, &kv_full[stage], 0, (int)(base + j * KV), colK / 8);
+                    tma_load_3d(sV, &tmkv, &kv_full[stage], 0, (int)(base + j * KV), colV / 8);
+                } else {
 #pragma unroll
-                for (int a = 0; a < Cfg::kAtoms; a++) {
-                    tma_load_2d(sK + a * Cfg::kAtomKV, &tmkv, &kv_full[stage], colK + 64 * a, (int)(base + j * KV));
-                    tma_load_2d(sV + a * Cfg::kAtomKV, &tmkv, &kv_full[stage], colV + 64 * a, (int)(base + j * KV));
+                    for (int a = 0; a < Cfg::kAtoms; a++) {
+                        tma_load_2d(sK + a * Cfg::kAtomKV, &tmkv, &kv_full[stage], colK + 64 * a,
+                                    (int)(base + j * KV));
+                        tma_load_2d(sV + a * Cfg::kAtomKV, &tmkv, &kv_full[stage], colV + 64 * a,
+                                    (int)(base + j * KV));
+                    }
                 }
                 issued |= 1u << stage;
                 last_par = (last_par & ~(1u << stage)) | (phase << stage);
@@ -296,9 +313,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
             constexpr uint32_t idesc_o = umma_idesc_f16_bmn(128, D);
             // descriptors built once, advanced by (byte offset >> 4) in their
             // start-address field (shared memory < 256 KB: no carry out of it)
-            const uint64_t q_desc = umma_desc_sw128(smem_u32(sQ));
-            const uint64_t k_desc0 = umma_desc_sw128(smem_u32(sKV));
-            const uint64_t v_desc0 = umma_desc_sw128_mn(smem_u32(sKV + Cfg::kTileKV), Cfg::kAtomKV);
+            // K-step advance per 16 columns / 16 keys, in 16-byte units (no-swizzle layout)
+            constexpr uint32_t kQStep = 2 * 128, kKStep = 2 * KV, kVStep = NS ? 16 : 128;
+            const uint64_t q_desc = NS ? umma_desc_noswz(smem_u32(sQ), 128 * 16, 128) : umma_desc_sw128(smem_u32(sQ));
+            const uint64_t k_desc0 =
+                NS ? umma_desc_noswz(smem_u32(sKV), KV * 16, 128) : umma_desc_sw128(smem_u32(sKV));
+            const uint64_t v_desc0 = NS ? umma_desc_noswz(smem_u32(sKV + Cfg::kTileKV), 128, KV * 16)
+                                        : umma_desc_sw128_mn(smem_u32(sKV + Cfg::kTileKV), Cfg::kAtomKV);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = mbar_wait(q_full, 0, err);
@@ -308,16 +329,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
                 const uint64_t so = (uint64_t)((stage * 2 * Cfg::kTileKV) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++) {
-                    const uint32_t oq = (kk / 4) * Cfg::kAtomQ + (kk % 4) * 32;
-                    const uint32_t ok_ = (kk / 4) * Cfg::kAtomKV + (kk % 4) * 32;
-                    umma_f16(tS, q_desc + (oq >> 4), k_desc0 + so + (ok_ >> 4), idesc_s, kk > 0);
+                    const uint32_t oq = NS ? kk * kQStep : ((kk / 4) * Cfg::kAtomQ + (kk % 4) * 32) >> 4;
+                    const uint32_t ok_ = NS ? kk * kKStep : ((kk / 4) * Cfg::kAtomKV + (kk % 4) * 32) >> 4;
+                    umma_f16(tS, q_desc + oq, k_desc0 + so + ok_, idesc_s, kk > 0);
                 }
                 umma_commit(s_full);
                 if (!mbar_wait(p_full, (uint32_t)j & 1u, err)) break;
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < KV / 16; kk++)
-                    umma_f16_tmem_a(tO, tS + (uint32_t)(kk * 8), v_desc0 + so + (uint64_t)(kk * 2048 >> 4), idesc_o,
+                    umma_f16_tmem_a(tO, tS + (uint32_t)(kk * 8), v_desc0 + so + (uint64_t)(kk * kVStep), idesc_o,
                                     (j > 0 || kk > 0));
                 umma_commit(&kv_empty[stage]);
                 if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
@@ -361,13 +382,15 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
             // O holds PV(0..j-1), complete (the S(j) commit covered it)
             if (j > 0 && __any_sync(0xffffffffu, raise)) {
 #pragma unroll
-                for (int a = 0; a < D / 32; a++) {
-                    float t[32];
-                    tmem_ld32(tO + lane_off + a * 32, t);
+                for (int a = 0; a < D / 16; a++) {        // 16-column steps: D = 80 is not a multiple of 32
+                    float t[16];
+                    tmem_ld16(tO + lane_off + a * 16, t);
+                    uint32_t u[16];
 #pragma unroll
-                    for (int i = 0; i < 32; i++) t[i] *= o_scale;
-                    tmem_st32(tO + lane_off + a * 32, t);
+                    for (int i = 0; i < 16; i++) u[i] = __float_as_uint(t[i] * o_scale);
+                    tmem_st16(tO + lane_off + a * 16, u);
                 }
+                tmem_wait_st();
             }
             // pass 2: P = 2^(s*scale - m*scale) in fp16 over S's first KV/2 columns
             const float ms = m * scale_log2;
@@ -410,18 +433,18 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
             const bool valid = q0 + row < T;
             __half* o = out + (base + q0 + row) * (long long)H + (long long)h * D;
 #pragma unroll
-            for (int a = 0; a < D / 32; a++) {
-                float t[32];
-                tmem_ld32(tO + lane_off + a * 32, t);
+            for (int a = 0; a < D / 16; a++) {
+                float t[16];
+                tmem_ld16(tO + lane_off + a * 16, t);
                 if (valid) {
 #pragma unroll
-                    for (int v = 0; v < 4; v++) {
+                    for (int v = 0; v < 2; v++) {
                         uint4 pk;
                         pk.x = pack_half2(t[8 * v + 0] * inv, t[8 * v + 1] * inv);
                         pk.y = pack_half2(t[8 * v + 2] * inv, t[8 * v + 3] * inv);
                         pk.z = pack_half2(t[8 * v + 4] * inv, t[8 * v + 5] * inv);
                         pk.w = pack_half2(t[8 * v + 6] * inv, t[8 * v + 7] * inv);
-                        *reinterpret_cast<uint4*>(o + a * 32 + v * 8) = pk;
+                        *reinterpret_cast<uint4*>(o + a * 16 + v * 8) = pk;
                     }
                 }
             }
@@ -447,37 +470,52 @@ static PFN_cuTensorMapEncodeTiled_v12000 attn_encode_fn() {
     return fn;
 }
 
-template <int D, int KV>
+template <int D, int KV, bool NS>
 static int launch_attn_tc(const void* qkv, void* out, const long long* off, const int* T, int n_utt, int H,
                           int n_heads, int max_T, long long M, int* err, cudaStream_t st) {
-    using Cfg = AttnTc<D, KV>;
+    using Cfg = AttnTc<D, KV, NS>;
     auto enc = attn_encode_fn();
     if (!enc) return W2V_ERR_DRIVER;
     // two views of qkv [M][3H]: 128-row boxes for Q, KV-row boxes for K and V
     CUtensorMap tmq, tmkv;
-    const uint64_t dims[2] = {(uint64_t)3 * H, (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)3 * H * 2};
-    const uint32_t es[2] = {1, 1};
-    const uint32_t boxq[2] = {64, 128}, boxkv[2] = {64, (uint32_t)KV};
-    if (enc(&tmq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(qkv), dims, strides, boxq, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
-        enc(&tmkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(qkv), dims, strides, boxkv, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return W2V_ERR_TENSOR_MAP;
+    CUresult r1, r2;
+    if constexpr (NS) {
+        // (8 columns, rows, 8-column chunks): boxes land as [chunk][row][16 B]
+        const uint64_t dims[3] = {8, (uint64_t)M, (uint64_t)3 * H / 8};
+        const uint64_t strides[2] = {(uint64_t)3 * H * 2, 16};
+        const uint32_t es[3] = {1, 1, 1};
+        const uint32_t boxq[3] = {8, 128, D / 8}, boxkv[3] = {8, (uint32_t)KV, D / 8};
+        r1 = enc(&tmq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(qkv), dims, strides, boxq, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        r2 = enc(&tmkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(qkv), dims, strides, boxkv, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        const uint64_t dims[2] = {(uint64_t)3 * H, (uint64_t)M};
+        const uint64_t strides[1] = {(uint64_t)3 * H * 2};
+        const uint32_t es[2] = {1, 1};
+        const uint32_t boxq[2] = {64, 128}, boxkv[2] = {64, (uint32_t)KV};
+        r1 = enc(&tmq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(qkv), dims, strides, boxq, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        r2 = enc(&tmkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(qkv), dims, strides, boxkv, es,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) return W2V_ERR_TENSOR_MAP;
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {
-        if (cudaFuncSetAttribute(attn_tc_kernel<D, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(attn_tc_kernel<D, KV, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Cfg::kSmem) != cudaSuccess)
             return W2V_ERR_LAUNCH;
         attr[dev & 63] = true;
     }
     const float scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     dim3 grid((max_T + 127) / 128, n_heads, n_utt);
-    attn_tc_kernel<D, KV><<<grid, 192, Cfg::kSmem, st>>>(tmq, tmkv, (__half*)out, off, T, H, scale_log2, err);
+    attn_tc_kernel<D, KV, NS><<<grid, 192, Cfg::kSmem, st>>>(tmq, tmkv, (__half*)out, off, T, H, scale_log2, err);
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
@@ -511,11 +549,14 @@ extern "C" int w2v_attention(const void* qkv, void* out, const long long* off, c
     const bool tma_ok = (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && H % 64 == 0;
     switch (d) {
         case 64:
-            if (tma_ok) return w2v::launch_attn_tc<64, 64>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+            if (tma_ok) return w2v::launch_attn_tc<64, 64, false>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
             return w2v::launch_attn<64>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
-        case 80: return w2v::launch_attn<80>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
+        case 80:
+            if ((reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && H % 8 == 0)
+                return w2v::launch_attn_tc<80, 64, true>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+            return w2v::launch_attn<80>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         case 128:
-            if (tma_ok) return w2v::launch_attn_tc<128, 64>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+            if (tma_ok) return w2v::launch_attn_tc<128, 64, false>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
             return w2v::launch_attn<128>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         default: return W2V_ERR_ARGS;
     }

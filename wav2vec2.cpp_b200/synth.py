@@ -60,6 +60,10 @@ ARCHS = {
     "tiny_pre": Arch("tiny_pre", conv_dim=128, feat_norm="layer", conv_bias=True, hidden=128,
                      n_layers=2, n_heads=2, ffn=256, pos_kernel=16, pos_groups=4, vocab=64,
                      stable_layer_norm=True),
+    # XLS-R-1B's head dim 80 and positional-conv group width 80 at small size
+    "tiny80": Arch("tiny80", conv_dim=128, feat_norm="layer", conv_bias=True, hidden=320,
+                   n_layers=2, n_heads=4, ffn=640, pos_kernel=16, pos_groups=4, vocab=64,
+                   stable_layer_norm=True),
 }
 
 
