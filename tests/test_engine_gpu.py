@@ -153,6 +153,23 @@ def test_batched_beam_overlaps_batches(W, model_path, synth):
         assert r["text"] == text and not r["words"]
 
 
+def test_pinned_inputs_upload_directly(W, model_path, synth):
+    """Page-locked caller buffers are copied to the device without staging;
+    logits and transcripts equal those of the same audio in pageable memory
+    (several upload chunks, an empty utterance included)."""
+    p = model_path("tiny", "q8_0", bias_std=0.02, gain_jitter=0.1)
+    m = model(W, p)
+    lens = [16000, 0, 7000, 12000, 3000, 9000, 16000, 400, 5000, 8000]
+    xs = [synth.make_audio(n, 200 + i) for i, n in enumerate(lens)]
+    keep = [torch.from_numpy(x).pin_memory() for x in xs]
+    pinned = [t.numpy() for t in keep]
+    a = m.logits(xs)
+    b = m.logits(pinned)
+    for u, v in zip(a, b):
+        assert u.shape == v.shape and np.array_equal(u, v)
+    assert [r["text"] for r in m.transcribe_batch(xs)] == [r["text"] for r in m.transcribe_batch(pinned)]
+
+
 def test_wav_file_transcribes_like_array(W, model_path, synth, tmp_path):
     """Audio ingestion feeding the engine: a 44.1 kHz stereo PCM16 file,
     decoded by wav2vec2_b200_load_wav, transcribes exactly like the decoded

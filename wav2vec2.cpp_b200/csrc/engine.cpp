@@ -659,9 +659,17 @@ void Engine::run_host(const std::vector<const float*>& audio, const std::vector<
     // queued behind that copy, so the DMA and packing of later chunks overlap
     // the convolutions of earlier ones.  The encoder then runs on the batch.
     const int B = g.n_utt;
+    // The first chunk is small (an eighth of the batch) so that the only
+    // upload nothing overlaps is short; the rest is split evenly.
     const int nch = B >= 32 ? kMaxChunks : B >= 8 ? 2 : 1;
     std::vector<int> cu(nch + 1);
-    for (int k = 0; k <= nch; k++) cu[k] = (int)((long long)B * k / nch);
+    cu[0] = 0;
+    if (nch == 1) {
+        cu[1] = B;
+    } else {
+        cu[1] = std::max(1, B / 8);
+        for (int k = 2; k <= nch; k++) cu[k] = cu[1] + (int)((long long)(B - cu[1]) * (k - 1) / (nch - 1));
+    }
     const int hw = (int)std::max(1u, std::thread::hardware_concurrency());
     const int nt = std::max(1, std::min({8, hw / 2, std::max(1, B / nch)}));
     std::unique_ptr<std::atomic<int>[]> packed(new std::atomic<int>[nch]);
@@ -675,7 +683,29 @@ void Engine::run_host(const std::vector<const float*>& audio, const std::vector<
             packed[k].fetch_add(1, std::memory_order_release);
         }
     };
-    if (fwd_begin(g, stream_)) {
+    // Page-locked caller buffers need no staging: each chunk's utterances are
+    // copied straight from them.
+    bool pinned = B > 0;
+    for (int u = 0; u < B && pinned; u++) {
+        if (!n_samples[u]) continue;
+        cudaPointerAttributes at{};
+        pinned = cudaPointerGetAttributes(&at, audio[u]) == cudaSuccess && at.type == cudaMemoryTypeHost;
+    }
+    cudaGetLastError();   // a pageable pointer may leave an error from the query
+    if (pinned && fwd_begin(g, stream_)) {
+        for (int k = 0; k < nch; k++) {
+            for (int u = cu[k]; u < cu[k + 1]; u++)
+                if (n_samples[u])
+                    cuda_check(cudaMemcpyAsync(audio_stage_.as<float>() + g.audio_off[u], audio[u],
+                                               (size_t)n_samples[u] * sizeof(float), cudaMemcpyHostToDevice,
+                                               copy_stream_),
+                               "audio upload");
+            cuda_check(cudaEventRecord(chunk_ev_[k], copy_stream_), "chunk event");
+            cuda_check(cudaStreamWaitEvent(stream_, chunk_ev_[k], 0), "chunk wait");
+            fwd_extract(audio_stage_.as<float>(), g, cu[k], cu[k + 1], stream_);
+        }
+        fwd_encode(g, stream_, nullptr, nullptr);
+    } else if (!pinned && fwd_begin(g, stream_)) {
         std::vector<std::thread> packers;
         struct Joiner {
             std::vector<std::thread>& v;
