@@ -341,12 +341,15 @@ def test_pos_conv(K, H, G, Kp):
         assert np.abs(got[off[u]:off[u] + t] - ref).max() < 2e-4 * (1 + np.abs(ref).max())
 
 
-@pytest.mark.parametrize("H,nh", [(768, 12), (1280, 16), (128, 2), (1024, 8), (64, 1)])
-def test_attention(K, H, nh):
+@pytest.mark.parametrize("H,nh,T", [(768, 12, [499, 1, 64, 65, 200]), (1280, 16, [499, 1, 64, 65, 200]),
+                                    (128, 2, [499, 1, 64, 65, 200]), (1024, 8, [499, 1, 64, 65, 200]),
+                                    (64, 1, [499, 1, 64, 65, 200]), (768, 12, [1499, 700]),
+                                    (1280, 16, [1499, 33]), (1024, 8, [1499, 257])])
+def test_attention(K, H, nh, T):
     """Flash attention vs fp64 softmax(QK^T/sqrt(d))V per utterance
-    (src/wav2vec2.cpp:304-334)."""
-    rng = np.random.default_rng(H)
-    T = [499, 1, 64, 65, 200]
+    (src/wav2vec2.cpp:304-334), up to 30 s utterances (T = 1499: 24 key tiles,
+    so the running max is raised mid-sequence)."""
+    rng = np.random.default_rng(H + len(T))
     off = np.concatenate([[0], np.cumsum(T)[:-1]]).astype(np.int64)
     M = sum(T)
     qkv = (rng.standard_normal((M, 3 * H)) * 1.5).astype(np.float16)
