@@ -74,6 +74,29 @@ def test_gemm_plain(K, M, N, Kd, epi, bn):
     assert (d <= tol).all(), f"max err {d.max().item()}"
 
 
+@pytest.mark.parametrize("bn", [0, -256])
+def test_gemm_gelu_epilogue_sweep(K, bn):
+    """The GELU epilogue over a dense sweep of inputs: row i of A holds x_i in
+    column 0 (exact in fp16), every weight row picks column 0, so each output
+    is gelu(x_i); compared with the tanh form in fp64."""
+    x = torch.linspace(-12, 12, 24001, device="cuda").half()
+    M, N, Kd = x.numel(), 64, 64
+    A = torch.zeros(M, Kd, device="cuda", dtype=torch.float16)
+    A[:, 0] = x
+    W = torch.zeros(N, Kd, device="cuda", dtype=torch.float16)
+    W[:, 0] = 1
+    out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float16)
+    err = err_word()
+    K.gemm(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, out.data_ptr(), N, M, M, 0, 0, N,
+           EPI_F16_GELU, bn, err.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = gelu_t(x.double())[:, None]
+    d = (out.double() - ref).abs()
+    assert (d <= 2e-3 * (1 + ref.abs())).all(), (d / (1 + ref.abs())).max().item()
+    assert (out[:, :1] == out).all(), "columns of one row differ"
+
+
 @pytest.mark.parametrize("M,N,Kd,epi,bn", [
     (1, 256, 64, EPI_F32, -256), (255, 256, 768, EPI_F16, -256), (257, 512, 768, EPI_F32_RESID, -256),
     (20000, 2304, 768, EPI_F16, -256), (9000, 768, 3072, EPI_F32_RESID, -256), (7777, 3072, 768, EPI_F16_GELU, -256),

@@ -232,6 +232,23 @@ W2V_DEV uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// gelu_tanh of two values, rounded to a packed fp16 pair: the tanh form
+// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) with the argument formed in
+// fp32 and tanh and the final multiply-add on fp16 pairs, one special-function
+// instruction for both values.  Error within 2e-3 (1 + |gelu(x)|), about twice
+// the fp16 rounding of the result it is stored as (the reference model, too,
+// evaluates GELU from a table indexed by the fp16 input).  Large |x|: the
+// argument saturates (tanh -> +-1), giving x or -0.
+W2V_DEV uint32_t gelu_half2(float a, float b) {
+    const uint32_t u = pack_half2(a * fmaf(a * a, 0.035677408f, 0.79788456f),
+                                  b * fmaf(b * b, 0.035677408f, 0.79788456f));
+    const uint32_t h = pack_half2(0.5f * a, 0.5f * b);
+    uint32_t t, o;
+    asm("tanh.approx.f16x2 %0, %1;" : "=r"(t) : "r"(u));
+    asm("fma.rn.f16x2 %0, %1, %2, %1;" : "=r"(o) : "r"(h), "r"(t));
+    return o;
+}
+
 }  // namespace w2v
 
 namespace w2v {

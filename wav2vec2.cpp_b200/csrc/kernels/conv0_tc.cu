@@ -198,8 +198,8 @@ __global__ void __launch_bounds__(kC0tThreads, 1) conv0_tc_kernel(Conv0TcArgs a)
                     const int r = rs + 4 * i;
                     if (f0 + r < F) {
                         uint2 pk;
-                        pk.x = pack_half2(gelu_tanh(fmaf(xs[i].x, sc[0], sh[0])), gelu_tanh(fmaf(xs[i].y, sc[1], sh[1])));
-                        pk.y = pack_half2(gelu_tanh(fmaf(xs[i].z, sc[2], sh[2])), gelu_tanh(fmaf(xs[i].w, sc[3], sh[3])));
+                        pk.x = gelu_half2(fmaf(xs[i].x, sc[0], sh[0]), fmaf(xs[i].y, sc[1], sh[1]));
+                        pk.y = gelu_half2(fmaf(xs[i].z, sc[2], sh[2]), fmaf(xs[i].w, sc[3], sh[3]));
                         *reinterpret_cast<uint2*>(orow0 + (long long)r * a.C + ch) = pk;
                     }
                 }

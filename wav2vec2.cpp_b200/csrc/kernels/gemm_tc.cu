@@ -221,9 +221,6 @@ W2V_DEV void epilogue_chunk_t(const GemmParams& p, const float* stg, long long o
     for (int i = 0; i < 8; i++) {
         float4& x = xs[i];
         x.x += b.x; x.y += b.y; x.z += b.z; x.w += b.w;
-        if (EPI == W2V_EPI_F16_GELU) {
-            x.x = gelu_tanh(x.x); x.y = gelu_tanh(x.y); x.z = gelu_tanh(x.z); x.w = gelu_tanh(x.w);
-        }
         if (EPI == W2V_EPI_F32_RESID) {
             x.x += res[i].x; x.y += res[i].y; x.z += res[i].z; x.w += res[i].w;
         }
@@ -245,13 +242,19 @@ W2V_DEV void epilogue_chunk_t(const GemmParams& p, const float* stg, long long o
             __half* c = reinterpret_cast<__half*>(p.C) + orow * p.ldc + col;
             if (full4) {
                 uint2 u;
-                u.x = pack_half2(x.x, x.y);
-                u.y = pack_half2(x.z, x.w);
+                if (EPI == W2V_EPI_F16_GELU) {
+                    u.x = gelu_half2(x.x, x.y);
+                    u.y = gelu_half2(x.z, x.w);
+                } else {
+                    u.x = pack_half2(x.x, x.y);
+                    u.y = pack_half2(x.z, x.w);
+                }
                 *reinterpret_cast<uint2*>(c) = u;
             } else {
-                c[0] = __float2half_rn(x.x);
-                if (col + 1 < p.N) c[1] = __float2half_rn(x.y);
-                if (col + 2 < p.N) c[2] = __float2half_rn(x.z);
+                const bool g = EPI == W2V_EPI_F16_GELU;
+                c[0] = __float2half_rn(g ? gelu_tanh(x.x) : x.x);
+                if (col + 1 < p.N) c[1] = __float2half_rn(g ? gelu_tanh(x.y) : x.y);
+                if (col + 2 < p.N) c[2] = __float2half_rn(g ? gelu_tanh(x.z) : x.z);
             }
         } else {
             float* c = reinterpret_cast<float*>(p.C) + orow * p.ldc + col;
