@@ -385,6 +385,13 @@ def run_kernel_case(args):
         res = out.data_ptr() if epi == 3 else 0
         fn = lambda: K.gemm(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, out.data_ptr(), N, M, M,
                             bias.data_ptr(), res, N, epi, args.block_n, 0, st)
+        if epi == 4:
+            # residual normalised on the fly from per-row (mean, rstd), in place over C
+            stats = torch.stack([torch.randn(M), torch.rand(M) + 0.5], 1).cuda()
+            lw, lb = torch.ones(N, device="cuda"), torch.zeros(N, device="cuda")
+            fn = lambda: K.gemm_ln_resid(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, out.data_ptr(),
+                                         N, M, M, bias.data_ptr(), out.data_ptr(), N, stats.data_ptr(),
+                                         lw.data_ptr(), lb.data_ptr(), block_n=args.block_n, stream=st)
         flops = 2.0 * M * N * Kd
     elif args.kernel == "attention":
         H, nh, T, B = 768, 12, 499, 64
@@ -403,7 +410,7 @@ def run_kernel_case(args):
         off = torch.arange(B, device="cuda", dtype=torch.int64) * T
         Tt = torch.full((B,), T, device="cuda", dtype=torch.int32)
         fn = lambda: K.pos_conv(out.data_ptr(), x.data_ptr(), off.data_ptr(), Tt.data_ptr(), B, H, Kp, G,
-                                wt.data_ptr(), bias.data_ptr(), T, st)
+                                wt.data_ptr(), bias.data_ptr(), T, 0, st)
         flops = 2.0 * B * T * Kp * (H // G) * H
     for _ in range(args.warmup):
         fn()
@@ -440,7 +447,8 @@ def main():
                     help="time one kernel at a representative size instead of the whole step")
     ap.add_argument("--rows", type=int, default=32768, help="GEMM rows for --kernel gemm")
     ap.add_argument("--gemm-shape", default="3072,768,1",
-                    help="N,K,epilogue for --kernel gemm (epilogue 0 fp16, 1 fp16+GELU, 2 fp32, 3 fp32+residual)")
+                    help="N,K,epilogue for --kernel gemm (epilogue 0 fp16, 1 fp16+GELU, 2 fp32, 3 fp32+residual, "
+                         "4 fp32+LayerNorm-normalised residual)")
     ap.add_argument("--block-n", type=int, default=0,
                     help="GEMM tile for --kernel gemm: 0 automatic, 64/128/256 one CTA, -128/-256 CTA pair")
     args = ap.parse_args()

@@ -233,21 +233,27 @@ W2V_DEV uint32_t pack_half2(float a, float b) {
 }
 
 // gelu_tanh of two values, rounded to a packed fp16 pair: the tanh form
-// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) with the argument formed in
-// fp32 and tanh and the final multiply-add on fp16 pairs, one special-function
-// instruction for both values.  Error within 2e-3 (1 + |gelu(x)|), about twice
-// the fp16 rounding of the result it is stored as (the reference model, too,
-// evaluates GELU from a table indexed by the fp16 input).  Large |x|: the
-// argument saturates (tanh -> +-1), giving x or -0.
-W2V_DEV uint32_t gelu_half2(float a, float b) {
-    const uint32_t u = pack_half2(a * fmaf(a * a, 0.035677408f, 0.79788456f),
-                                  b * fmaf(b * b, 0.035677408f, 0.79788456f));
-    const uint32_t h = pack_half2(0.5f * a, 0.5f * b);
-    uint32_t t, o;
+// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) evaluated entirely on fp16
+// pairs once x is rounded to fp16 (as the reference model does: it evaluates
+// GELU from a table indexed by the fp16 input), six pair instructions and one
+// of them on the special-function unit.  Error within 2e-3 (1 + |gelu(x)|),
+// about twice the fp16 rounding of the result.  Large |x|: x^2 and the tanh
+// argument saturate to +-inf (tanh -> +-1), giving x or 0.
+W2V_DEV uint32_t gelu_f16x2(uint32_t x) {
+    const uint32_t c0 = 0x3a623a62u;   // sqrt(2/pi) in fp16, both halves
+    const uint32_t c1 = 0x28912891u;   // 0.044715 sqrt(2/pi)
+    const uint32_t half = 0x38003800u; // 0.5
+    uint32_t x2, p, u, t, h, o;
+    asm("mul.rn.f16x2 %0, %1, %1;" : "=r"(x2) : "r"(x));
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(p) : "r"(x2), "r"(c1), "r"(c0));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(u) : "r"(x), "r"(p));
     asm("tanh.approx.f16x2 %0, %1;" : "=r"(t) : "r"(u));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(h) : "r"(x), "r"(half));
     asm("fma.rn.f16x2 %0, %1, %2, %1;" : "=r"(o) : "r"(h), "r"(t));
     return o;
 }
+
+W2V_DEV uint32_t gelu_half2(float a, float b) { return gelu_f16x2(pack_half2(a, b)); }
 
 }  // namespace w2v
 
