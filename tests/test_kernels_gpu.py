@@ -293,7 +293,8 @@ def test_conv0_norm_gelu(K, synth, norm):
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     got = out.float().cpu().numpy()
-    assert (got[:, int(frames.max()):] == 0).all(), "rows past the frames were written"
+    for u in range(len(lens)):
+        assert (got[u, frames[u]:] == 0).all(), f"rows past utterance {u}'s frames were written"
     for u, x in enumerate(audio):
         xd = x.astype(np.float64)
         xn = ((x - np.float32(xd.mean())) * np.float32(1 / np.sqrt(np.float32(xd.var()) + 1e-7))).astype(np.float32)
@@ -305,6 +306,50 @@ def test_conv0_norm_gelu(K, synth, norm):
         ref = np.vectorize(O.gelu)(y) if y.size < 2000 else 0.5 * y * (1 + np.tanh(0.7978845608028654 * (y + 0.044715 * y ** 3)))
         g_u = got[u, :frames[u]]
         assert np.abs(g_u - ref).max() <= 2e-3 * (1 + np.abs(ref).max()), np.abs(g_u - ref).max()
+
+
+@pytest.mark.parametrize("C", [512, 256])
+def test_conv0_many_short_utterances(K, synth, C):
+    """Tensor-core conv layer 0 (GroupNorm) over 300 short utterances, some
+    empty: every CTA walks several (utterance, channel-half) groups, so the
+    folded-weight buffers and the output boxes are each reused many times.
+    Rows past each utterance's frames stay untouched."""
+    k0, s0 = 10, 5
+    rng = np.random.default_rng(C)
+    lens = [int(n) for n in rng.integers(0, 1400, 300)]
+    lens[3] = 4      # shorter than the kernel: no frames
+    lens[7] = 650    # 129 frames: one full block and one frame
+    audio = [synth.make_audio(n, 7 + i) if n else np.zeros(0, np.float32) for i, n in enumerate(lens)]
+    off, ln, frames = _meta(lens)
+    w0 = (rng.standard_normal((C, 1, k0)) * 0.02).astype(np.float32)
+    b0 = (rng.standard_normal(C) * 0.01).astype(np.float32)
+    gw = (1 + rng.standard_normal(C) * 0.1).astype(np.float32)
+    gb = (rng.standard_normal(C) * 0.02).astype(np.float32)
+    d_audio, d_off, d_len, d_fr = dev(np.concatenate(audio)), dev(off), dev(ln), dev(frames)
+    d_w0, d_b0, d_gw, d_gb = dev(w0.reshape(C, k0)), dev(b0), dev(gw), dev(gb)
+    n = len(lens)
+    stats = torch.empty(2 * n, device="cuda")
+    gn = torch.empty(n * C * 2, device="cuda", dtype=torch.float64)
+    rows = int(frames.max()) + 3
+    out = torch.zeros(n, rows, C, device="cuda", dtype=torch.float16)
+    err = err_word()
+    K.wave_stats(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), n, stats.data_ptr(), stream())
+    K.conv0(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), d_fr.data_ptr(), n, stats.data_ptr(),
+            d_w0.data_ptr(), d_b0.data_ptr(), C, k0, s0, 1, d_gw.data_ptr(), d_gb.data_ptr(), gn.data_ptr(),
+            out.data_ptr(), rows, int(frames.max()), err.data_ptr(), stream())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = out.float().cpu().numpy()
+    for u, x in enumerate(audio):
+        assert (got[u, frames[u]:] == 0).all(), f"rows past utterance {u}'s frames were written"
+        if frames[u] == 0:
+            continue
+        xd = x.astype(np.float64)
+        xn = ((x - np.float32(xd.mean())) * np.float32(1 / np.sqrt(np.float32(xd.var()) + 1e-7))).astype(np.float32)
+        y = O.group_norm(O.conv1d(xn[:, None], w0, b0, stride=s0), gw, gb)
+        ref = 0.5 * y * (1 + np.tanh(0.7978845608028654 * (y + 0.044715 * y ** 3)))
+        d = np.abs(got[u, :frames[u]] - ref).max()
+        assert d <= 2e-3 * (1 + np.abs(ref).max()), (u, d)
 
 
 @pytest.mark.parametrize("D,f16in,gelu", [(768, 0, 0), (512, 1, 1), (1280, 0, 0), (128, 1, 0)])

@@ -108,6 +108,27 @@ W2V_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* m, uint64_t* bar, in
         : "memory");
 }
 
+// Tile store shared -> global (no multicast); completion tracked per thread
+// through bulk async-groups.  Coordinates must be non-negative and the
+// innermost one a multiple of 16 bytes.
+W2V_DEV void tma_store_3d(const CUtensorMap* m, const void* smem_src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+W2V_DEV void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's committed groups still read shared memory.
+template <int N>
+W2V_DEV void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N of this thread's committed groups are incomplete.
+template <int N>
+W2V_DEV void bulk_wait_group() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ── tcgen05 (5th-gen tensor cores, accumulators in TMEM) ────────────────────
 W2V_DEV void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
