@@ -130,12 +130,15 @@ def test_gemm_cta_pair(K, M, N, Kd, epi, bn):
     assert torch.isnan(out[M:]).all(), "rows past m_valid were written"
 
 
+@pytest.mark.parametrize("N,ldc", [(94, 104), (200, 216)])
 @pytest.mark.parametrize("epi", [EPI_F16_GELU, EPI_F32_RESID])
 @pytest.mark.parametrize("bn", [0, 128, 192, -256, -192])
-def test_gemm_ragged_columns(K, epi, bn):
-    """N not a multiple of 4 inside a wider row pitch: the last column group
-    of each row is stored element by element, columns N..ldc-1 untouched."""
-    M, N, Kd, ldc = 700, 94, 256, 104
+def test_gemm_ragged_columns(K, epi, bn, N, ldc):
+    """N not a multiple of the tile width inside a wider row pitch, columns
+    N..ldc-1 untouched: N = 94 (not a multiple of 4: the last column group
+    of each row is stored element by element) and N = 200 (fp16 C through
+    TMA tile stores clipped at column N)."""
+    M, Kd = 700, 256
     g = torch.Generator(device="cuda").manual_seed(5)
     A = torch.randn(M, Kd, device="cuda", generator=g).half()
     W = (torch.randn(N, Kd, device="cuda", generator=g) * 0.05).half()

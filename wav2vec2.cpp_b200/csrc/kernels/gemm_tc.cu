@@ -46,6 +46,7 @@ __host__ __device__ constexpr int fit_stages(int want, int stage_bytes, int fixe
 
 struct GemmParams {
     int vec;              // 16-byte vector stores/loads are aligned for this C / resid
+    int tma_c;            // fp16 C is written by TMA tile stores (tensor map tmC)
     int kb_per_tap;       // Cin / 64
     int conv_stride;      // s (1 for plain GEMMs)
     int m_valid;          // valid rows per batch
@@ -305,9 +306,69 @@ W2V_DEV void epilogue_warp(const GemmParams& p, uint32_t tmem_row, float* stg, l
     __syncwarp();
 }
 
+// fp16 epilogues with a TMA-store-able C: each 32 x 32 chunk goes, as fp16,
+// into one of the warp's two 2 KB boxes (32 rows of 64 bytes, 64-byte swizzle:
+// 16-byte group j of row r at j ^ ((r >> 1) & 3), so the row-per-thread
+// writes are bank-conflict free) and leaves by one TMA tile store.  The
+// tensor map's bounds (N columns, m_valid rows per batch) clip ragged tiles.
+// nst counts this warp's stores (box parity); a box is rewritten only after
+// the store issued from it two stores earlier has read it.
+template <int EPI>
+W2V_DEV void epilogue_warp_tma(const GemmParams& p, const CUtensorMap* tmC, uint32_t tmem_row, uint8_t* box0,
+                               int row0, int b, int col_base, int c0, int c1, uint32_t& nst) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll 1
+    for (int c = c0; c < c1; c++) {
+        const int col0 = col_base + c * 32;
+        if (col0 >= p.N) break;
+        float v[32];
+        tmem_ld32(tmem_row + (uint32_t)(c * 32), v);
+        if (p.bias) {
+            if (col0 + 32 <= p.N) {
+                const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float4 bb = __ldg(b4 + j);
+                    v[4 * j] += bb.x; v[4 * j + 1] += bb.y; v[4 * j + 2] += bb.z; v[4 * j + 3] += bb.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j++) if (col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
+            }
+        }
+        uint8_t* box = box0 + (nst & 1u) * 2048;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            uint4 pk;
+            if (EPI == W2V_EPI_F16_GELU) {
+                pk.x = gelu_half2(v[8 * j + 0], v[8 * j + 1]);
+                pk.y = gelu_half2(v[8 * j + 2], v[8 * j + 3]);
+                pk.z = gelu_half2(v[8 * j + 4], v[8 * j + 5]);
+                pk.w = gelu_half2(v[8 * j + 6], v[8 * j + 7]);
+            } else {
+                pk.x = pack_half2(v[8 * j + 0], v[8 * j + 1]);
+                pk.y = pack_half2(v[8 * j + 2], v[8 * j + 3]);
+                pk.z = pack_half2(v[8 * j + 4], v[8 * j + 5]);
+                pk.w = pack_half2(v[8 * j + 6], v[8 * j + 7]);
+            }
+            *reinterpret_cast<uint4*>(box + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = pk;
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_3d(tmC, box, col0, row0, b);
+            bulk_commit_group();
+        }
+        nst++;
+    }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(gemm_threads(EPI), 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, GemmParams p) {
     constexpr int NE = epi_warps(EPI);
     using Cfg = GemmCfg<BN, NE>;
     constexpr int S = Cfg::kStages;
@@ -402,6 +463,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         constexpr int kNch = BN / 32, kParts = NE / 4;
         const int cb = part * kNch / kParts, ce = (part + 1) * kNch / kParts;
         float* stg = stage_buf + (warp - 2) * 32 * 32;
+        constexpr bool kF16 = EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU;
+        uint32_t nst = 0;   // TMA stores issued by this warp
         int it = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, it++) {
             const int ni = tile % p.n_tiles;
@@ -420,11 +483,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (EPI == W2V_EPI_F32_RESID_LN) load_ln_stats_t(p, out_row0, row0, lst);
             if (!mbar_wait(&tfull[ab], aph, p.err)) break;
             tc_fence_after();
-            epilogue_warp<EPI>(p, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN), stg, out_row0, row0,
-                               ni * BN, c0, ce, res, lst);
+            const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+            if constexpr (kF16) {
+                if (p.tma_c)
+                    epilogue_warp_tma<EPI>(p, &tmC, trow, reinterpret_cast<uint8_t*>(stg), row0, b, ni * BN, c0, ce,
+                                           nst);
+                else
+                    epilogue_warp<EPI>(p, trow, stg, out_row0, row0, ni * BN, c0, ce, res, lst);
+            } else {
+                epilogue_warp<EPI>(p, trow, stg, out_row0, row0, ni * BN, c0, ce, res, lst);
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[ab]);
+        }
+        if (kF16 && p.tma_c) {   // the stores are complete before the CTA exits
+            if (lane == 0) bulk_wait_group<0>();
+            __syncwarp();
         }
     }
 
@@ -463,7 +538,8 @@ struct Gemm2Cfg {
 
 template <int BN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm_threads(EPI), 1)
-gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, GemmParams p) {
     constexpr int NE = epi_warps(EPI);
     using Cfg = Gemm2Cfg<BN, NE>;
     constexpr int S = Cfg::kStages;
@@ -580,6 +656,8 @@ gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         const int cb = part * kNch / kParts, ce = (part + 1) * kNch / kParts;
         const uint32_t tempty_lead = mapa_shared(smem_u32(tempty), 0);
         float* stg = stage_buf + (warp - 2) * 32 * 32;
+        constexpr bool kF16 = EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU;
+        uint32_t nst = 0;   // TMA stores issued by this warp
         int it = 0;
         for (int tile = pair; tile < total; tile += n_pairs, it++) {
             const int ni = tile % p.n_tiles;
@@ -597,11 +675,23 @@ gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             if (EPI == W2V_EPI_F32_RESID_LN) load_ln_stats_t(p, out_row0, row0, lst);
             if (!mbar_wait(&tfull[ab], aph, p.err)) break;
             tc_fence_after();
-            epilogue_warp<EPI>(p, tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN), stg, out_row0, row0,
-                               ni * BN, c0, ce, res, lst);
+            const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+            if constexpr (kF16) {
+                if (p.tma_c)
+                    epilogue_warp_tma<EPI>(p, &tmC, trow, reinterpret_cast<uint8_t*>(stg), row0, b, ni * BN, c0, ce,
+                                           nst);
+                else
+                    epilogue_warp<EPI>(p, trow, stg, out_row0, row0, ni * BN, c0, ce, res, lst);
+            } else {
+                epilogue_warp<EPI>(p, trow, stg, out_row0, row0, ni * BN, c0, ce, res, lst);
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_lead + (uint32_t)(ab * 8));
+        }
+        if (kF16 && p.tma_c) {   // the stores are complete before the CTA exits
+            if (lane == 0) bulk_wait_group<0>();
+            __syncwarp();
         }
     }
 
@@ -664,7 +754,8 @@ static int sm_count() {
 }
 
 template <int BN, int EPI>
-static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
+static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
+                     cudaStream_t st) {
     using Cfg = GemmCfg<BN, epi_warps(EPI)>;
     auto kern = gemm_tc_kernel<BN, EPI>;
     static bool attr_set[64] = {};
@@ -677,7 +768,7 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPar
     }
     const int total = p.n_batch * p.m_tiles * p.n_tiles;
     const int grid = total < sm_count() ? total : sm_count();
-    kern<<<grid, gemm_threads(EPI), Cfg::kSmem, st>>>(ta, tb, p);
+    kern<<<grid, gemm_threads(EPI), Cfg::kSmem, st>>>(ta, tb, tc, p);
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
@@ -705,7 +796,8 @@ static int max_pairs(int dev) {
 }
 
 template <int BN, int EPI>
-static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
+static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmParams& p,
+                       cudaStream_t st) {
     using Cfg = Gemm2Cfg<BN, epi_warps(EPI)>;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -713,20 +805,21 @@ static int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmP
     if (mp <= 0) return W2V_ERR_LAUNCH;
     const int total = p.n_batch * p.m_tiles * p.n_tiles;
     const int pairs = total < mp ? total : mp;
-    gemm2_tc_kernel<BN, EPI><<<2 * pairs, gemm_threads(EPI), Cfg::kSmem, st>>>(ta, tb, p);
+    gemm2_tc_kernel<BN, EPI><<<2 * pairs, gemm_threads(EPI), Cfg::kSmem, st>>>(ta, tb, tc, p);
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
 template <int EPI>
-static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
+static int launch_epi(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                      const GemmParams& p, cudaStream_t st) {
     switch (bn) {
-        case 256: return launch_bn<256, EPI>(ta, tb, p, st);
-        case 192: return launch_bn<192, EPI>(ta, tb, p, st);
-        case 128: return launch_bn<128, EPI>(ta, tb, p, st);
-        case -256: return launch_pair<256, EPI>(ta, tb, p, st);
-        case -192: return launch_pair<192, EPI>(ta, tb, p, st);
-        case -128: return launch_pair<128, EPI>(ta, tb, p, st);
-        default: return launch_bn<64, EPI>(ta, tb, p, st);
+        case 256: return launch_bn<256, EPI>(ta, tb, tc, p, st);
+        case 192: return launch_bn<192, EPI>(ta, tb, tc, p, st);
+        case 128: return launch_bn<128, EPI>(ta, tb, tc, p, st);
+        case -256: return launch_pair<256, EPI>(ta, tb, tc, p, st);
+        case -192: return launch_pair<192, EPI>(ta, tb, tc, p, st);
+        case -128: return launch_pair<128, EPI>(ta, tb, tc, p, st);
+        default: return launch_bn<64, EPI>(ta, tb, tc, p, st);
     }
 }
 
@@ -835,20 +928,39 @@ static int gemm_impl(const void* A, long long a_cin, int a_taps, int a_stride, l
     const uint32_t bbox[2] = {kBK, (uint32_t)(bn < 0 ? -bn / 2 : bn)};
     rc = make_map_f16(&tb, B, 2, bdims, bstr, bbox);
     if (rc) return rc;
+    // fp16 C by TMA tile stores: [n_batch][c_batch_rows][ldc], rows m_valid and
+    // columns N in bounds, boxes of 32 x 32 (64-byte swizzle).  A store clips
+    // the innermost dimension at 16-byte granularity only (a partly covered
+    // 16-byte group is written whole), so N must be a multiple of 8.
+    CUtensorMap tc = tb;
+    p.tma_c = 0;
+    if ((epilogue == W2V_EPI_F16 || epilogue == W2V_EPI_F16_GELU) && p.vec && ldc % 8 == 0 && N % 8 == 0 &&
+        (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+        auto enc = get_encode();
+        if (!enc) return W2V_ERR_DRIVER;
+        const uint64_t cdims[3] = {(uint64_t)N, (uint64_t)m_valid, (uint64_t)a_batches};
+        const uint64_t cstr[2] = {(uint64_t)ldc * 2, (uint64_t)c_batch_rows * ldc * 2};
+        const uint32_t cbox[3] = {32, 32, 1}, ces[3] = {1, 1, 1};
+        if (enc(&tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, C, cdims, cstr, cbox, ces, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return W2V_ERR_TENSOR_MAP;
+        p.tma_c = 1;
+    }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     switch (epilogue) {
-        case W2V_EPI_F16: return launch_epi<W2V_EPI_F16>(bn, ta, tb, p, st);
-        case W2V_EPI_F16_GELU: return launch_epi<W2V_EPI_F16_GELU>(bn, ta, tb, p, st);
-        case W2V_EPI_F32: return launch_epi<W2V_EPI_F32>(bn, ta, tb, p, st);
+        case W2V_EPI_F16: return launch_epi<W2V_EPI_F16>(bn, ta, tb, tc, p, st);
+        case W2V_EPI_F16_GELU: return launch_epi<W2V_EPI_F16_GELU>(bn, ta, tb, tc, p, st);
+        case W2V_EPI_F32: return launch_epi<W2V_EPI_F32>(bn, ta, tb, tc, p, st);
         case W2V_EPI_F32_RESID:
             if (!resid) return W2V_ERR_ARGS;
-            return launch_epi<W2V_EPI_F32_RESID>(bn, ta, tb, p, st);
+            return launch_epi<W2V_EPI_F32_RESID>(bn, ta, tb, tc, p, st);
         case W2V_EPI_F32_RESID_LN:
             if (!resid || !ln_stats || !ln_w || !ln_b || !p.vec ||
                 ((reinterpret_cast<uintptr_t>(ln_stats) | reinterpret_cast<uintptr_t>(ln_w) |
                   reinterpret_cast<uintptr_t>(ln_b)) & 15))
                 return W2V_ERR_ARGS;
-            return launch_epi<W2V_EPI_F32_RESID_LN>(bn, ta, tb, p, st);
+            return launch_epi<W2V_EPI_F32_RESID_LN>(bn, ta, tb, tc, p, st);
         default: return W2V_ERR_ARGS;
     }
 }
