@@ -179,27 +179,28 @@ attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, const long
 
 // ── tcgen05 flash attention (head dim 64 or 128) ────────────────────────────
 // One CTA per (utterance, head, 128-query tile); 192 threads:
-//   warp 0      TMA: Q once, then K/V tiles of KV keys through a 2-stage ring
-//   warp 1      one thread issues tcgen05.mma: S = Q K^T into TMEM, then
-//               O += P V with P read from TMEM (A operand) and V straight from
-//               its TMA tile as an MN-major shared-memory operand
+//   warp 0      TMA: Q once, then K/V tiles of KV keys through a kStages ring
+//   warp 1      one thread issues tcgen05.mma: S = Q K^T into one of two TMEM
+//               S buffers, then O += P V with P read from TMEM (A operand)
+//               and V straight from its TMA tile as an MN-major operand
 //   warps 2..5  softmax, one query row per thread (its TMEM lane), in two
 //               passes over S (row max, then 2^x and P) so only 32 scores
 //               are live in registers; P is packed to fp16 over the first
-//               KV/2 columns of S (each 32-score chunk is read before the 16
-//               columns it overwrites).
+//               KV/2 columns of its S buffer (each 32-score chunk is read
+//               before the 16 columns it overwrites).
 // The running max used as the exponent reference is only raised when the
 // row max exceeds it by more than 2^8 (in the exp2 domain): P then stays
 // <= 256 (exact in fp16 range) and the O rescale in TMEM is rare.  The sum
 // and O use the same reference, so the result is unchanged.
-// Ordering: one thread issues every MMA, in order: PV(j) (which reads P(j)
-// from S's columns) before S(j+1) (which overwrites them).  Every S(j)
-// commit also covers PV(j-1), so once the softmax sees S(j) it may rescale
-// O and write P; the MMA issues PV(j) only after the softmax has published
-// P(j).  Handoffs use mbarriers with bounded waits.
-// TMEM: S/P at columns 0..KV-1, O at KV..KV+D-1.  With KV = 64 and D = 64 a
-// CTA holds 128 columns and 50 KB of shared memory, so four CTAs share an SM
-// and hide each other's handoff latencies.
+// Pipeline: S(j+1) is computed into the other buffer while the softmax works
+// on S(j).  The single MMA thread issues, in order, S(0), then per tile j:
+// S(j+1), [wait for P(j)], PV(j).  PV(j) reads P(j) from buffer j & 1 before
+// S(j+2) overwrites it (in-order execution); S(j) completing implies PV(j-2)
+// has.  A softmax that must rescale O at tile j first waits for PV(j-1)
+// (pv_done), so O then holds PV(0..j-1).  Handoffs use mbarriers with
+// bounded waits.
+// TMEM: S buffers at columns 0..KV-1 and KV..2KV-1, O at 2KV..2KV+D-1: 256
+// columns, so two CTAs share an SM; the K/V ring is as deep as that allows.
 template <int D, int KV, bool NS = false>
 struct AttnTc {
     static constexpr int kAtoms = NS ? 1 : D / 64;      // 64-column swizzle atoms per row
@@ -207,11 +208,13 @@ struct AttnTc {
     static constexpr int kTileKV = KV * D * 2;          // one K or V tile
     static constexpr int kAtomQ = 128 * 128;            // 128 rows x 128 B
     static constexpr int kAtomKV = KV * 128;
-    static constexpr int kStages = 2;
+    static constexpr int kColO = 2 * KV;
+    static constexpr int kTmemCols = 2 * KV + D <= 128 ? 128 : 2 * KV + D <= 256 ? 256 : 512;
+    static constexpr int kMinBlocks = kTmemCols <= 128 ? 4 : kTmemCols <= 256 ? 2 : 1;
+    // K/V stages: as many as kMinBlocks CTAs per SM leave room for, 2..4
+    static constexpr int kFit = ((228 * 1024) / kMinBlocks - 1024 - kTileQ - 1024 - 128) / (2 * kTileKV);
+    static constexpr int kStages = kFit > 4 ? 4 : kFit < 2 ? 2 : kFit;
     static constexpr int kSmem = kTileQ + kStages * 2 * kTileKV + 1024 + 128;
-    static constexpr int kColO = KV;
-    static constexpr int kTmemCols = KV + D <= 128 ? 128 : KV + D <= 256 ? 256 : 512;
-    static constexpr int kMinBlocks = kTmemCols <= 128 ? 4 : 2;
 };
 
 constexpr float kLazyRescaleLog2 = 8.f;
@@ -244,17 +247,20 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
     uint64_t* q_full = bars;
     uint64_t* kv_full = bars + 1;                     // [kStages]
     uint64_t* kv_empty = bars + 1 + Cfg::kStages;     // [kStages]
-    uint64_t* s_full = bars + 1 + 2 * Cfg::kStages;
-    uint64_t* p_full = s_full + 1;
-    uint64_t* o_full = s_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 3);
+    uint64_t* s_full = bars + 1 + 2 * Cfg::kStages;   // [2] one per S buffer
+    uint64_t* p_full = s_full + 2;
+    uint64_t* pv_done = s_full + 3;
+    uint64_t* o_full = s_full + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 5);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int s = 0; s < Cfg::kStages; s++) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
-        mbar_init(s_full, 1);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
         mbar_init(p_full, 4);
+        mbar_init(pv_done, 1);
         mbar_init(o_full, 1);
         fence_mbar_init();
         tma_prefetch_desc(&tmq);
@@ -265,7 +271,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t tS = tmem_base, tO = tmem_base + Cfg::kColO;
+    const uint32_t tO = tmem_base + Cfg::kColO;
     const int colQ = h * D, colK = H + h * D, colV = 2 * H + h * D;
 
     if (warp == 0) {
@@ -320,28 +326,41 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
                 NS ? umma_desc_noswz(smem_u32(sKV), KV * 16, 128) : umma_desc_sw128(smem_u32(sKV));
             const uint64_t v_desc0 = NS ? umma_desc_noswz(smem_u32(sKV + Cfg::kTileKV), 128, KV * 16)
                                         : umma_desc_sw128_mn(smem_u32(sKV + Cfg::kTileKV), Cfg::kAtomKV);
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = mbar_wait(q_full, 0, err);
-            for (int j = 0; j < n_kv && ok; j++) {
-                if (!mbar_wait(&kv_full[stage], phase, err)) break;
-                tc_fence_after();
-                const uint64_t so = (uint64_t)((stage * 2 * Cfg::kTileKV) >> 4);
+            // S(i) = Q K(i)^T into S buffer i & 1, from K/V stage i % kStages
+            auto issue_s = [&](int i) {
+                const uint64_t so = (uint64_t)(((i % Cfg::kStages) * 2 * Cfg::kTileKV) >> 4);
+                const uint32_t tSi = tmem_base + (uint32_t)((i & 1) * KV);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++) {
                     const uint32_t oq = NS ? kk * kQStep : ((kk / 4) * Cfg::kAtomQ + (kk % 4) * 32) >> 4;
                     const uint32_t ok_ = NS ? kk * kKStep : ((kk / 4) * Cfg::kAtomKV + (kk % 4) * 32) >> 4;
-                    umma_f16(tS, q_desc + oq, k_desc0 + so + ok_, idesc_s, kk > 0);
+                    umma_f16(tSi, q_desc + oq, k_desc0 + so + ok_, idesc_s, kk > 0);
                 }
-                umma_commit(s_full);
+                umma_commit(&s_full[i & 1]);
+            };
+            bool ok = mbar_wait(q_full, 0, err) && mbar_wait(&kv_full[0], 0, err);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0);
+            }
+            for (int j = 0; j < n_kv && ok; j++) {
+                if (j + 1 < n_kv) {
+                    if (!mbar_wait(&kv_full[(j + 1) % Cfg::kStages], (uint32_t)((j + 1) / Cfg::kStages) & 1u, err))
+                        break;
+                    tc_fence_after();
+                    issue_s(j + 1);
+                }
                 if (!mbar_wait(p_full, (uint32_t)j & 1u, err)) break;
                 tc_fence_after();
+                const int sj = j % Cfg::kStages;
+                const uint64_t so = (uint64_t)((sj * 2 * Cfg::kTileKV) >> 4);
+                const uint32_t tSj = tmem_base + (uint32_t)((j & 1) * KV);
 #pragma unroll
                 for (int kk = 0; kk < KV / 16; kk++)
-                    umma_f16_tmem_a(tO, tS + (uint32_t)(kk * 8), v_desc0 + so + (uint64_t)(kk * kVStep), idesc_o,
+                    umma_f16_tmem_a(tO, tSj + (uint32_t)(kk * 8), v_desc0 + so + (uint64_t)(kk * kVStep), idesc_o,
                                     (j > 0 || kk > 0));
-                umma_commit(&kv_empty[stage]);
-                if (++stage == Cfg::kStages) { stage = 0; phase ^= 1u; }
+                umma_commit(pv_done);
+                umma_commit(&kv_empty[sj]);
             }
             umma_commit(o_full);   // also reached on error: completes once the issued MMAs have
         }
@@ -353,16 +372,22 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
         float m = -INFINITY, l = 0.f;                  // exponent reference (raw score units) and row sum
         bool ok = true;
         for (int j = 0; j < n_kv && ok; j++) {
-            if (!mbar_wait(s_full, (uint32_t)j & 1u, err)) { ok = false; break; }
+            const uint32_t tS = tmem_base + (uint32_t)((j & 1) * KV);   // this tile's S buffer
+            if (!mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, err)) { ok = false; break; }
             tc_fence_after();
             const int nvalid = T - j * KV < KV ? T - j * KV : KV;   // keys of this tile inside the utterance
             const bool full = nvalid == KV;
-            // pass 1: row max
+            // pass 1: row max (a single 32-score chunk stays in registers for pass 2)
             float mx = -INFINITY;
+            float t1[32];
 #pragma unroll
             for (int c = 0; c < kChunks; c++) {
                 float t[32];
                 tmem_ld32(tS + lane_off + c * 32, t);
+                if constexpr (kChunks == 1) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) t1[i] = t[i];
+                }
                 if (full) {
 #pragma unroll
                     for (int i = 0; i < 32; i++) mx = fmaxf(mx, t[i]);
@@ -379,8 +404,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
                 l *= o_scale;
                 m = mx;
             }
-            // O holds PV(0..j-1), complete (the S(j) commit covered it)
+            // rescale O once it holds PV(0..j-1)
             if (j > 0 && __any_sync(0xffffffffu, raise)) {
+                if (!mbar_wait(pv_done, (uint32_t)(j - 1) & 1u, err)) { ok = false; break; }
+                tc_fence_after();
 #pragma unroll
                 for (int a = 0; a < D / 16; a++) {        // 16-column steps: D = 80 is not a multiple of 32
                     float t[16];
@@ -398,7 +425,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
 #pragma unroll
             for (int c = 0; c < kChunks; c++) {
                 float t[32];
-                tmem_ld32(tS + lane_off + c * 32, t);
+                if constexpr (kChunks == 1) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) t[i] = t1[i];
+                } else {
+                    tmem_ld32(tS + lane_off + c * 32, t);
+                }
                 uint32_t pk[16];
                 if (full) {
 #pragma unroll
@@ -549,14 +581,14 @@ extern "C" int w2v_attention(const void* qkv, void* out, const long long* off, c
     const bool tma_ok = (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && H % 64 == 0;
     switch (d) {
         case 64:
-            if (tma_ok) return w2v::launch_attn_tc<64, 64, false>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+            if (tma_ok) return w2v::launch_attn_tc<64, 32, false>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
             return w2v::launch_attn<64>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         case 80:
             if ((reinterpret_cast<uintptr_t>(qkv) & 15) == 0 && H % 8 == 0)
-                return w2v::launch_attn_tc<80, 64, true>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+                return w2v::launch_attn_tc<80, 32, true>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
             return w2v::launch_attn<80>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         case 128:
-            if (tma_ok) return w2v::launch_attn_tc<128, 64, false>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
+            if (tma_ok) return w2v::launch_attn_tc<128, 32, false>(qkv, out, off, T, n_utt, H, n_heads, max_T, M, err, st);
             return w2v::launch_attn<128>(qkv, out, off, T, n_utt, H, n_heads, max_T, st);
         default: return W2V_ERR_ARGS;
     }
