@@ -389,8 +389,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
                     for (int i = 0; i < 32; i++) t1[i] = t[i];
                 }
                 if (full) {
+                    float m0 = mx, m1 = t[0];
 #pragma unroll
-                    for (int i = 0; i < 32; i++) mx = fmaxf(mx, t[i]);
+                    for (int i = 1; i < 29; i += 4) {   // t[1] .. t[28]
+                        m0 = max3f(m0, t[i], t[i + 1]);
+                        m1 = max3f(m1, t[i + 2], t[i + 3]);
+                    }
+                    mx = max3f(max3f(m0, m1, t[29]), t[30], t[31]);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; i++)
@@ -433,14 +438,18 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
                 }
                 uint32_t pk[16];
                 if (full) {
+                    // pairs: (s * scale - m * scale) and the running sums two at a time
+                    const uint64_t sc2 = f32x2(scale_log2, scale_log2), nm2 = f32x2(-ms, -ms);
+                    uint64_t s2 = f32x2(sum0, sum1);
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
-                        const float p0 = ex2_sfu(fmaf(t[i], scale_log2, -ms));
-                        const float p1 = ex2_sfu(fmaf(t[i + 1], scale_log2, -ms));
-                        sum0 += p0;
-                        sum1 += p1;
+                        float y0, y1;
+                        f32x2_split(fma_f32x2(f32x2(t[i], t[i + 1]), sc2, nm2), y0, y1);
+                        const float p0 = ex2_sfu(y0), p1 = ex2_sfu(y1);
+                        s2 = add_f32x2(s2, f32x2(p0, p1));
                         pk[i / 2] = pack_half2(p0, p1);
                     }
+                    f32x2_split(s2, sum0, sum1);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
