@@ -197,8 +197,14 @@ attn_kernel(const __half* __restrict__ qkv, __half* __restrict__ out, const long
 // S(j+1), [wait for P(j)], PV(j).  PV(j) reads P(j) from buffer j & 1 before
 // S(j+2) overwrites it (in-order execution); S(j) completing implies PV(j-2)
 // has.  A softmax that must rescale O at tile j first waits for PV(j-1)
-// (pv_done), so O then holds PV(0..j-1).  Handoffs use mbarriers with
-// bounded waits.
+// (pv_done), so O then holds PV(0..j-1).  P(j) is published on p_full[j & 1]:
+// S(j+1) is ready before PV(j) is issued, so a softmax warp can finish tile
+// j+1 while another is still on tile j, and with one barrier its second
+// arrival would complete tile j's phase early.  With one P barrier per S
+// buffer a warp is at most one tile ahead (S(j+2) waits for PV(j), which
+// waits for every warp's P(j)), and every arrival, s_full and pv_done phase
+// is at most one phase from the one its waiter expects.  Handoffs use
+// mbarriers with bounded waits.
 // TMEM: S buffers at columns 0..KV-1 and KV..2KV-1, O at 2KV..2KV+D-1: 256
 // columns, so two CTAs share an SM; the K/V ring is as deep as that allows.
 template <int D, int KV, bool NS = false>
@@ -248,10 +254,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
     uint64_t* kv_full = bars + 1;                     // [kStages]
     uint64_t* kv_empty = bars + 1 + Cfg::kStages;     // [kStages]
     uint64_t* s_full = bars + 1 + 2 * Cfg::kStages;   // [2] one per S buffer
-    uint64_t* p_full = s_full + 2;
-    uint64_t* pv_done = s_full + 3;
-    uint64_t* o_full = s_full + 4;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 5);
+    uint64_t* p_full = s_full + 2;                    // [2] one per S buffer
+    uint64_t* pv_done = s_full + 4;
+    uint64_t* o_full = s_full + 5;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 6);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -259,7 +265,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
         for (int s = 0; s < Cfg::kStages; s++) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
         mbar_init(&s_full[0], 1);
         mbar_init(&s_full[1], 1);
-        mbar_init(p_full, 4);
+        mbar_init(&p_full[0], 4);
+        mbar_init(&p_full[1], 4);
         mbar_init(pv_done, 1);
         mbar_init(o_full, 1);
         fence_mbar_init();
@@ -350,7 +357,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
                     tc_fence_after();
                     issue_s(j + 1);
                 }
-                if (!mbar_wait(p_full, (uint32_t)j & 1u, err)) break;
+                if (!mbar_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u, err)) break;
                 tc_fence_after();
                 const int sj = j % Cfg::kStages;
                 const uint64_t so = (uint64_t)((sj * 2 * Cfg::kTileKV) >> 4);
@@ -466,9 +473,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ 
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[j & 1]);
         }
-        if (ok && mbar_wait(o_full, 0, err)) {
+        // o_full is committed on every path once the issued MMAs complete: wait
+        // for it even after an expired wait, so TMEM is never freed under an MMA
+        if (mbar_wait(o_full, 0, err) && ok) {
             tc_fence_after();
             const float inv = __fdividef(1.f, l);
             const bool valid = q0 + row < T;

@@ -310,13 +310,16 @@ W2V_DEV void epilogue_warp(const GemmParams& p, uint32_t tmem_row, float* stg, l
 // into one of the warp's two 2 KB boxes (32 rows of 64 bytes, 64-byte swizzle:
 // 16-byte group j of row r at j ^ ((r >> 1) & 3), so the row-per-thread
 // writes are bank-conflict free) and leaves by one TMA tile store.  The
-// tensor map's bounds (N columns, m_valid rows per batch) clip ragged tiles.
-// nst counts this warp's stores (box parity); a box is rewritten only after
-// the store issued from it two stores earlier has read it.
+// tensor map's bounds (N columns, m_valid rows per batch) clip the rows and
+// columns of a box that starts inside the tensor; a box that would start past
+// the last row (lane quarters beyond m_valid in the last row tile) is never
+// stored.  nst counts this warp's stores (box parity); a box is rewritten
+// only after the store issued from it two stores earlier has read it.
 template <int EPI>
 W2V_DEV void epilogue_warp_tma(const GemmParams& p, const CUtensorMap* tmC, uint32_t tmem_row, uint8_t* box0,
                                int row0, int b, int col_base, int c0, int c1, uint32_t& nst) {
     const int lane = threadIdx.x & 31;
+    if (row0 >= p.m_valid) return;   // every row of this warp's quarter is past the end
 #pragma unroll 1
     for (int c = c0; c < c1; c++) {
         const int col0 = col_base + c * 32;
