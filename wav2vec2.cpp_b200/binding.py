@@ -180,12 +180,14 @@ class Model:
                                              len(audios), C.cast(res, _vp))
         if rc:
             raise EngineError(last_error())
+        free = lib().wav2vec2_result_free
         out = []
         for r in res:
             c = r.contents
-            words = [(c.words[i].text.decode(), c.words[i].t_start, c.words[i].t_end) for i in range(c.n_words)]
+            nw = c.n_words
+            words = [(w.text.decode(), w.t_start, w.t_end) for w in c.words[:nw]] if nw else []
             out.append({"text": c.transcript.decode(), "n_frames": c.n_frames, "words": words})
-            lib().wav2vec2_result_free(r)
+            free(r)
         return out
 
     def transcribe(self, audio, beam_size: int = 1, word_timestamps: bool = False) -> dict:

@@ -19,9 +19,11 @@
 //   warp 0      TMA producer: STAGES-deep smem ring, mbarrier full/empty.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
 //   warps 2..   epilogue (8 warps for fp32 / residual outputs, 12 for fp16
-//               ones): tcgen05.ld -> bias / GELU / residual -> global;
-//               two or three warps per TMEM lane quarter, each taking a
-//               contiguous share of the tile's columns.
+//               ones): tcgen05.ld -> bias / GELU / residual -> global (fp16
+//               C through per-warp TMA tile stores where its layout allows,
+//               fp32 C through the staged coalesced stores below); two or
+//               three warps per TMEM lane quarter, each taking a contiguous
+//               share of the tile's columns.
 // Every mbarrier wait is bounded (common.cuh); on expiry the kernel records
 // an error code and returns.
 #include "common.cuh"
@@ -145,7 +147,7 @@ W2V_DEV void epilogue_chunk(const GemmParams& p, long long out_row, long long re
     }
 }
 
-// ── coalesced epilogue ──────────────────────────────────────────────────────
+// ── coalesced epilogue (fp32 outputs, and fp16 ones TMA cannot store) ──────
 // tcgen05.ld 32x32b gives a thread one row; storing that directly makes each
 // warp instruction touch 32 rows.  Instead each epilogue warp stages its
 // 32 x 32 fp32 chunk in a private 4 KB shared buffer (float4 groups XOR-
