@@ -446,6 +446,63 @@ def test_attention(K, H, nh, T):
         assert np.abs(got[sl] - ref).max() < 4e-3, np.abs(got[sl] - ref).max()
 
 
+@pytest.mark.parametrize("N,Kd,epi", [(2304, 768, EPI_F16), (768, 3072, EPI_F32)])
+def test_gemm_repeated_launches_identical(K, N, Kd, epi):
+    """The CTA-pair GEMM hands stages and accumulators between its TMA,
+    MMA and epilogue warps (and across the pair) through mbarriers; a
+    handshake that loses a phase shows up only under timing skew.  30
+    launches at an encoder shape (31936 rows, automatic tile) must give
+    bitwise the same output and no expired wait."""
+    M = 31936
+    g = torch.Generator(device="cuda").manual_seed(N + Kd)
+    A = torch.randn(M, Kd, device="cuda", generator=g).half()
+    W = (torch.randn(N, Kd, device="cuda", generator=g) * 0.05).half()
+    bias = torch.randn(N, device="cuda", generator=g)
+    dt = torch.float16 if epi == EPI_F16 else torch.float32
+    outs = [torch.zeros(M, N, device="cuda", dtype=dt) for _ in range(2)]
+    err = err_word()
+    for r in range(30):
+        K.gemm(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, outs[r % 2].data_ptr(), N, M, M,
+               bias.data_ptr(), 0, N, epi, 0, err.data_ptr(), stream())
+        if r % 2:
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0, f"launch {r}: expired wait"
+            assert torch.equal(outs[0], outs[1]), f"launch {r} differs from launch {r - 1}"
+
+
+def test_conv0_repeated_launches_identical(K, synth):
+    """Tensor-core conv layer 0 at the benchmark's batch (64 x 10 s): each
+    CTA folds per-utterance weights into two shared buffers that it reuses
+    once the MMAs reading them are done, and stores through TMA boxes it
+    reuses once their stores have read them.  10 launches must give bitwise
+    the same output and no expired wait."""
+    C, k0, s0, n = 512, 10, 5, 64
+    lens = [160000] * n
+    audio = np.concatenate([synth.make_audio(L, 500 + i) for i, L in enumerate(lens)])
+    off, ln, frames = _meta(lens)
+    rng = np.random.default_rng(3)
+    w0 = (rng.standard_normal((C, k0)) * 0.02).astype(np.float32)
+    b0 = (rng.standard_normal(C) * 0.01).astype(np.float32)
+    gw = (1 + rng.standard_normal(C) * 0.1).astype(np.float32)
+    gb = (rng.standard_normal(C) * 0.02).astype(np.float32)
+    d_audio, d_off, d_len, d_fr = dev(audio), dev(off), dev(ln), dev(frames)
+    d_w0, d_b0, d_gw, d_gb = dev(w0), dev(b0), dev(gw), dev(gb)
+    stats = torch.empty(2 * n, device="cuda")
+    gn = torch.empty(n * C * 2, device="cuda", dtype=torch.float64)
+    rows = int(frames.max())
+    outs = [torch.zeros(n, rows, C, device="cuda", dtype=torch.float16) for _ in range(2)]
+    err = err_word()
+    K.wave_stats(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), n, stats.data_ptr(), stream())
+    for r in range(10):
+        K.conv0(d_audio.data_ptr(), d_off.data_ptr(), d_len.data_ptr(), d_fr.data_ptr(), n, stats.data_ptr(),
+                d_w0.data_ptr(), d_b0.data_ptr(), C, k0, s0, 1, d_gw.data_ptr(), d_gb.data_ptr(), gn.data_ptr(),
+                outs[r % 2].data_ptr(), rows, rows, err.data_ptr(), stream())
+        if r % 2:
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0, f"launch {r}: expired wait"
+            assert torch.equal(outs[0], outs[1]), f"launch {r} differs from launch {r - 1}"
+
+
 @pytest.mark.parametrize("H,nh", [(768, 12), (1024, 16)])
 def test_attention_repeated_launches_identical(K, H, nh):
     """The softmax warps and the MMA thread hand S and P tiles back and forth
