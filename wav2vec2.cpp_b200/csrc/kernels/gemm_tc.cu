@@ -18,12 +18,11 @@
 // Roles (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: STAGES-deep smem ring, mbarrier full/empty.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
-//   warps 2..   epilogue (8 warps for fp32 / residual outputs, 12 for fp16
-//               ones): tcgen05.ld -> bias / GELU / residual -> global (fp16
+//   warps 2..9  epilogue: tcgen05.ld -> bias / GELU / residual -> global (fp16
 //               C through per-warp TMA tile stores where its layout allows,
-//               fp32 C through the staged coalesced stores below); two or
-//               three warps per TMEM lane quarter, each taking a contiguous
-//               share of the tile's columns.
+//               fp32 C through the staged coalesced stores below); two
+//               warps per TMEM lane quarter, each taking half of the tile's
+//               columns.
 // Every mbarrier wait is bounded (common.cuh); on expiry the kernel records
 // an error code and returns.
 #include "common.cuh"
@@ -34,12 +33,12 @@ namespace w2v {
 constexpr int kBM = 128;       // tile rows (UMMA M)
 constexpr int kBK = 64;        // K per stage (128 B of fp16: one swizzle row)
 constexpr int kUmmaK = 16;     // K per tcgen05.mma kind::f16
-// Epilogue warps: 12 (three per TMEM lane quarter) for the fp16 epilogues,
-// whose GELU / conversion work per element is the longest; 8 for the fp32
-// residual epilogues, which hold a prefetched residual chunk in registers.
-__host__ __device__ constexpr int epi_warps(int epi) {
-    return (epi == W2V_EPI_F16 || epi == W2V_EPI_F16_GELU) ? 12 : 8;
-}
+// Epilogue warps: 8 (two per TMEM lane quarter) for every epilogue.  The
+// fp16 ones (TMA tile stores, GELU on fp16 pairs) are short enough that more
+// warps buy nothing, while the 4 KB of staging a warp holds is shared memory
+// the TMA ring can use: at 8 warps a CTA pair with 256-wide tiles keeps six
+// stages in flight instead of five (QKV 96.2 -> 93.7 us at 31936 rows).
+__host__ __device__ constexpr int epi_warps(int) { return 8; }
 __host__ __device__ constexpr int gemm_threads(int epi) { return 64 + 32 * epi_warps(epi); }
 constexpr int kSmemCap = 232448;        // opt-in dynamic shared memory per block on sm_100
 __host__ __device__ constexpr int fit_stages(int want, int stage_bytes, int fixed_bytes) {
