@@ -1,7 +1,7 @@
 """End-to-end parity of the engine (C API) against the oracle and against
 golden outputs of the reference's own forward pass.
 
-Tolerances (north-star): logits max-abs 2e-2 for Q8_0/F16 weights and 5e-2
+Tolerances: logits max-abs 2e-2 for Q8_0/F16 weights and 5e-2
 for Q4_0, against the reference path with exact fp32 linears.  Against the
 reference's ggml-emulated path (activations re-quantised to Q8_0 inside every
 linear) the gap is dominated by that quantisation itself; those comparisons
