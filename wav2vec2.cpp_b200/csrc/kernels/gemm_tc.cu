@@ -387,7 +387,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t* empty = bars + S;
     uint64_t* tfull = bars + 2 * S;
     uint64_t* tempty = bars + 2 * S + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+    uint64_t* done = bars + 2 * S + 4;    // every MMA this CTA issued has completed (teardown)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int total = p.n_batch * p.m_tiles * p.n_tiles;
@@ -395,6 +396,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], NE); }
+        mbar_init(done, 1);
         fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
@@ -458,6 +460,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
                 if (ok) umma_commit(&tfull[ab]);
             }
+            // no MMA may still be writing TMEM when it is freed (also after an expired wait)
+            umma_commit(done);
+            mbar_wait(done, 0, p.err);
         }
         __syncwarp();
     } else {
