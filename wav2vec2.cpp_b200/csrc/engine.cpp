@@ -197,6 +197,7 @@ Engine::~Engine() {
                           &L.ln2b})
             rel(*b);
     if (h_audio_) cudaFreeHost(h_audio_);
+    if (h_out_) cudaFreeHost(h_out_);
     prof_fold();
     for (auto e : ev_pool_) cudaEventDestroy(e);
     if (meta_done_) cudaEventDestroy(meta_done_);
@@ -730,28 +731,45 @@ void Engine::run_host(const std::vector<const float*>& audio, const std::vector<
         for (auto& t : packers) t.join();
         fwd_encode(g, stream_, nullptr, nullptr);
     }
-    if (g.M > 0) {
-        if (logits) {
-            logits->resize((size_t)g.M * cfg_.vocab);
-            cuda_check(cudaMemcpyAsync(logits->data(), logits_.p, logits->size() * 4, cudaMemcpyDeviceToHost, stream_),
-                       "logits download");
-        }
-        if (spans) {
-            spans->resize((size_t)g.M * 3);
-            cuda_check(cudaMemcpyAsync(spans->data(), spans_.p, spans->size() * 4, cudaMemcpyDeviceToHost, stream_),
-                       "spans download");
-        }
+    if (g.M > 0 && logits) {
+        logits->resize((size_t)g.M * cfg_.vocab);
+        cuda_check(cudaMemcpyAsync(logits->data(), logits_.p, logits->size() * 4, cudaMemcpyDeviceToHost, stream_),
+                   "logits download");
+    }
+    // The device error word, the spans and the span counts come back through
+    // one pinned staging buffer and one synchronisation.
+    const size_t sp_bytes = spans && g.M > 0 ? (size_t)g.M * 3 * sizeof(int) : 0;
+    const size_t ns_bytes = n_spans && g.M > 0 ? (size_t)g.n_utt * sizeof(int) : 0;
+    const size_t out_bytes = 16 + sp_bytes + ns_bytes;
+    if (out_bytes > h_out_n_) {
+        cuda_check(cudaStreamSynchronize(stream_), "sync");
+        if (h_out_) cudaFreeHost(h_out_);
+        h_out_ = nullptr;
+        cuda_check(cudaMallocHost(&h_out_, out_bytes), "cudaMallocHost");
+        h_out_n_ = out_bytes;
+    }
+    cuda_check(cudaMemcpyAsync(h_out_, err_.p, sizeof(int), cudaMemcpyDeviceToHost, stream_), "error word download");
+    if (sp_bytes)
+        cuda_check(cudaMemcpyAsync(h_out_ + 16, spans_.p, sp_bytes, cudaMemcpyDeviceToHost, stream_), "spans download");
+    if (ns_bytes)
+        cuda_check(cudaMemcpyAsync(h_out_ + 16 + sp_bytes, nspans_.p, ns_bytes, cudaMemcpyDeviceToHost, stream_),
+                   "spans download");
+    cuda_check(cudaStreamSynchronize(stream_), "forward");
+    int e = 0;
+    memcpy(&e, h_out_, sizeof(int));
+    if (e) {
+        cudaMemsetAsync(err_.p, 0, sizeof(int), stream_);
+        cudaStreamSynchronize(stream_);
+        throw std::runtime_error("device error " + std::to_string(e) + " (bounded wait expired)");
+    }
+    if (spans && g.M > 0) {
+        spans->resize((size_t)g.M * 3);
+        memcpy(spans->data(), h_out_ + 16, sp_bytes);
     }
     if (n_spans) {
         n_spans->assign(g.n_utt, 0);
-        if (g.M > 0)
-            cuda_check(cudaMemcpyAsync(n_spans->data(), nspans_.p, (size_t)g.n_utt * 4, cudaMemcpyDeviceToHost,
-                                       stream_),
-                       "spans download");
+        if (ns_bytes) memcpy(n_spans->data(), h_out_ + 16 + sp_bytes, ns_bytes);
     }
-    cuda_check(cudaStreamSynchronize(stream_), "forward");
-    const int e = check_device_error();
-    if (e) throw std::runtime_error("device error " + std::to_string(e) + " (bounded wait expired)");
     if (geom_out) *geom_out = std::move(g);
 }
 

@@ -155,6 +155,8 @@ private:
     // pinned host staging
     float* h_audio_ = nullptr;
     size_t h_audio_n_ = 0;
+    uint8_t* h_out_ = nullptr;                 // pinned: error word, spans and span counts of a host batch
+    size_t h_out_n_ = 0;
     std::vector<uint8_t> meta_host_;
     cudaEvent_t meta_done_ = nullptr;
     // host-batch uploads: a copy stream and one event per utterance chunk
