@@ -60,9 +60,19 @@ def peaks():
     return PEAKS_FALLBACK, "fallback (profiling recipe)"
 
 
+def encoder_frames(n_samples: int) -> int:
+    """Encoder frames of an utterance under the base model's conv stack
+    (kernel, stride) = (10, 5), (3, 2) x 4, (2, 2) x 2."""
+    n = n_samples
+    for k, s in ((10, 5), (3, 2), (3, 2), (3, 2), (3, 2), (2, 2), (2, 2)):
+        n = (n - k) // s + 1 if n >= k else 0
+    return n
+
+
 def workload(args) -> dict:
+    n = int(args.seconds * SR)
     return {"workload": f"wav2vec2-base {args.dtype.upper()} (seeded random init), {args.batch} utterances x "
-                        f"{args.seconds:g} s per GPU ({int(args.seconds * SR)} samples, 499 frames each), greedy CTC",
+                        f"{args.seconds:g} s per GPU ({n} samples, {encoder_frames(n)} frames each), greedy CTC",
             "per_gpu_batch": args.batch, "global_batch": args.batch * args.world,
             "utterance_seconds": args.seconds, "linears": args.dtype,
             "parallelism": f"dp{args.world} (utterances sharded per GPU, no collective on the data path)",
@@ -309,49 +319,63 @@ def run_ours(args):
                    "sample": "unavailable: oracle/_ref build absent"}
 
     if rank == 0:
-        audio_per_step = args.batch * args.seconds
-        value = world * args.steps * audio_per_step / (elapsed_ms / 1000.0)
-        pk, pk_src = peaks()
-        g = prof.get("gemm_encoder", {"ms": 0, "launches": 0, "flops": 0})
-        achieved = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] else 0.0
-        peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
-        total_flops = sum(v["flops"] for v in prof.values())
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
-            "config": workload(args),
-            "roofline": {"bound": "tensor",
-                         "kernel": "gemm_tc_kernel / gemm2_tc_kernel on the encoder linears (tcgen05, TMEM)",
-                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak if peak else None,
-                         "traffic": encoder_gemm_traffic(args),
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of each "
-                                           "encoder linear at this workload, mean per launch",
-                         "peak_source": f"bf16 dense sustained, {pk_src}",
-                         "frac_of_burst_peak": achieved / pk["bf16_tflops"] if pk.get("bf16_tflops") else None,
-                         "launches": g["launches"], "avg_launch_ms": g["ms"] / max(1, g["launches"]),
-                         "flops_per_launch": g["flops"] / max(1, g["launches"])},
-            "step_tflops": total_flops / steps_prof / (elapsed_ms / args.steps / 1000.0) / 1e12,
-            "breakdown_ms_per_step": {k: v["ms"] / steps_prof for k, v in prof.items()},
-            "gpu_launches": launches * args.steps * world,
-            "clocks": {"sm_mhz": all_clocks[0].get("sm_mhz"), "sm_max_mhz": all_clocks[0].get("sm_max_mhz"),
-                       "reasons": sorted(set(r for c in all_clocks for r in c.get("reasons", []))),
-                       "samples": all_clocks[0].get("samples"),
-                       "per_rank_sm_mhz": [c.get("sm_mhz") for c in all_clocks]},
-        }
-        if e2e_s:
-            line["e2e"] = {"value": world * args.e2e_steps * audio_per_step / e2e_s, "unit": UNIT,
-                           "h2d_bytes_per_step": args.batch * n * 4,
-                           "d2h_bytes_per_step": 499 * args.batch * 3 * 4 + args.batch * 4,
-                           "steps": args.e2e_steps, "api": "wav2vec2_transcribe_batch (pinned host float32 in, text out)"}
-        if cpu:
-            line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
+        print(json.dumps(result_line(args, world, elapsed_ms, prof, steps_prof, launches, all_clocks, e2e_s, cpu)),
+              flush=True)
     m.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def result_line(args, world, elapsed_ms, prof, steps_prof, launches, all_clocks, e2e_s, cpu) -> dict:
+    """The benchmark's JSON line from its measurements: elapsed_ms over
+    args.steps timed steps (max over ranks), prof the per-category event
+    times of steps_prof profiled steps ({name: {"ms", "launches", "flops"}}),
+    launches per forward, one clock record per rank, e2e_s seconds for
+    args.e2e_steps calls of the public batch API (0 or None: not measured),
+    cpu the CPU-baseline record or None."""
+    n = int(args.seconds * SR)
+    audio_per_step = args.batch * args.seconds
+    value = world * args.steps * audio_per_step / (elapsed_ms / 1000.0)
+    pk, pk_src = peaks()
+    g = prof.get("gemm_encoder", {"ms": 0, "launches": 0, "flops": 0})
+    achieved = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] else 0.0
+    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    total_flops = sum(v["flops"] for v in prof.values())
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
+        "config": workload(args),
+        "roofline": {"bound": "tensor",
+                     "kernel": "gemm_tc_kernel / gemm2_tc_kernel on the encoder linears (tcgen05, TMEM)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak if peak else None,
+                     "traffic": encoder_gemm_traffic(args),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of each "
+                                       "encoder linear at this workload, mean per launch",
+                     "peak_source": f"bf16 dense sustained, {pk_src}",
+                     "frac_of_burst_peak": achieved / pk["bf16_tflops"] if pk.get("bf16_tflops") else None,
+                     "launches": g["launches"], "avg_launch_ms": g["ms"] / max(1, g["launches"]),
+                     "flops_per_launch": g["flops"] / max(1, g["launches"])},
+        "step_tflops": total_flops / steps_prof / (elapsed_ms / args.steps / 1000.0) / 1e12,
+        "breakdown_ms_per_step": {k: v["ms"] / steps_prof for k, v in prof.items()},
+        "gpu_launches": launches * args.steps * world,
+        "clocks": {"sm_mhz": all_clocks[0].get("sm_mhz"), "sm_max_mhz": all_clocks[0].get("sm_max_mhz"),
+                   "reasons": sorted(set(r for c in all_clocks for r in c.get("reasons", []))),
+                   "samples": all_clocks[0].get("samples"),
+                   "per_rank_sm_mhz": [c.get("sm_mhz") for c in all_clocks]},
+    }
+    if e2e_s:
+        # per step: the pinned float32 audio in; spans (3 ints per frame), span counts and the
+        # device error word out
+        line["e2e"] = {"value": world * args.e2e_steps * audio_per_step / e2e_s, "unit": UNIT,
+                       "h2d_bytes_per_step": args.batch * n * 4,
+                       "d2h_bytes_per_step": encoder_frames(n) * args.batch * 3 * 4 + args.batch * 4 + 4,
+                       "steps": args.e2e_steps, "api": "wav2vec2_transcribe_batch (pinned host float32 in, text out)"}
+    if cpu:
+        line["cpu_baseline"] = cpu
+    return line
 
 
 # DRAM bytes per launch of the four encoder linears of wav2vec2-base at 64 x
