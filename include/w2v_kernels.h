@@ -111,8 +111,12 @@ int w2v_conv0(const float* audio, const long long* off, const int* len, const in
  *   (and nothing is launched).
  *   It calls no cudaMalloc/cudaFree.  The first call on a device looks the
  *   buffer's device address up once (make that first call before any stream
- *   capture).  All calls on a device share the buffer: calls that overlap on
- *   the GPU (different streams, no ordering) race on it. */
+ *   capture).  Under CUDA's default lazy module loading that first lookup may
+ *   also load the library's device code, which allocates device memory and
+ *   can block: make one warm-up call per device from a thread that is
+ *   allowed to block (not the real-time thread) and outside stream capture.
+ *   All calls on a device share the buffer: calls that overlap on the GPU
+ *   (different streams, no ordering) race on it. */
 int w2v_conv0_noalloc(const float* audio, const long long* off, const int* len, const int* frames,
                       int n_utt, const float* stats, const float* w0, const float* b0, int C, int k0,
                       int s0, int norm, const float* gw, const float* gb, void* out, long long rows_max,

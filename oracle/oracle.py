@@ -20,7 +20,7 @@ ORACLE_DIR = Path(__file__).resolve().parent
 LIB = ORACLE_DIR / "liboracle.so"
 REF_LIB = ORACLE_DIR / "_ref" / "libw2v_ref.so"
 REF_CLI = ORACLE_DIR / "_ref" / "wav2vec2-cli"
-REF_SRC = Path("/root/reference")
+REF_SRC = Path(os.environ.get("W2V_REFERENCE", "/root/reference"))
 
 EXACT, GGML = 0, 1
 _vp = ctypes.c_void_p

@@ -3,6 +3,7 @@ declared symbol, the model loader rejects bad files before touching a GPU,
 the public header matches the reference's, and the batch planner /
 fault-tolerant scheduler behave (simulated device failures re-queue work)."""
 import json
+import os
 import re
 import subprocess
 from pathlib import Path
@@ -12,7 +13,7 @@ import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 INC = ROOT / "include"
-REF_HDR = Path("/root/reference/include/wav2vec2.h")
+REF_HDR = Path(os.environ.get("W2V_REFERENCE", "/root/reference")) / "include" / "wav2vec2.h"
 
 
 def declared_functions(header: Path) -> set[str]:
@@ -41,6 +42,18 @@ def test_library_exports_every_declared_symbol(B):
             assert hasattr(L, n), f"{n} declared in {h} is not exported"
         for n in names:
             assert n in B.SIGNATURES, f"{n} has no ctypes signature in binding.py"
+
+
+@pytest.mark.parametrize("C", [0, -4])
+def test_conv0_rejects_non_positive_channels(B, C):
+    """Channel counts <= 0 are rejected by the argument check, before any CUDA
+    call (so this runs without a GPU), by both conv layer 0 entry points."""
+    L = B.lib()
+    W2V_ERR_ARGS = 1
+    assert L.w2v_conv0(None, None, None, None, 4, None, None, None, C, 10, 5, 1, None, None, None, None, 1, 1,
+                       None, None) == W2V_ERR_ARGS
+    assert L.w2v_conv0_noalloc(None, None, None, None, 4, None, None, None, C, 10, 5, 1, None, None, None, 1, 1,
+                               None, None) == W2V_ERR_ARGS
 
 
 def test_public_header_matches_reference_api():

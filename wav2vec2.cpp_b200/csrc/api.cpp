@@ -395,6 +395,16 @@ int wav2vec2_transcribe_batch(wav2vec2_context* ctx, wav2vec2_params params, con
                             }
                             return;
                         }
+                        // The batch's results are assembled locally and published
+                        // only once all of them exist: if one throws, the batch is
+                        // re-queued and nothing already built is left behind.
+                        struct Local {
+                            std::vector<wav2vec2_result*> r;
+                            ~Local() {
+                                for (auto* p : r) wav2vec2_result_free(p);
+                            }
+                        } local;
+                        local.r.assign(nb, nullptr);
                         for (int j = 0; j < nb; j++) {
                             const int T = g.T[j];
                             std::vector<Span> sp;
@@ -406,8 +416,12 @@ int wav2vec2_transcribe_batch(wav2vec2_context* ctx, wav2vec2_params params, con
                             }
                             std::vector<Word> words;
                             if (params.word_timestamps) words = spans_to_words(sp, c);
-                            results[b[j]] = make_result(c, T, ids_to_text(ids, c),
-                                                        params.word_timestamps ? &words : nullptr);
+                            local.r[j] = make_result(c, T, ids_to_text(ids, c),
+                                                     params.word_timestamps ? &words : nullptr);
+                        }
+                        for (int j = 0; j < nb; j++) {
+                            results[b[j]] = local.r[j];
+                            local.r[j] = nullptr;
                         }
                     });
         if (pool) pool->finish();

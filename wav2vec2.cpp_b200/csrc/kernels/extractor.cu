@@ -786,7 +786,8 @@ extern "C" int w2v_conv0(const float* audio, const long long* off, const int* le
                          const float* stats, const float* w0, const float* b0, int C, int k0, int s0, int norm,
                          const float* gw, const float* gb, double* gn_sums, void* out, long long rows_max,
                          int max_frames, int* err, void* stream) {
-    if (C > 512 || C % 2 || k0 > kC0MaxK || k0 <= 0 || s0 <= 0 || norm < 0 || norm > 2) return W2V_ERR_ARGS;
+    if (C <= 0 || C > 512 || C % 2 || k0 > kC0MaxK || k0 <= 0 || s0 <= 0 || norm < 0 || norm > 2)
+        return W2V_ERR_ARGS;
     if ((norm == 1 && !gn_sums) || (norm && (!gw || !gb))) return W2V_ERR_ARGS;
     if (n_utt <= 0 || max_frames <= 0) return W2V_OK;
     Conv0Args a{audio, off, len, frames, stats, w0, b0, C, k0, s0, norm, gw, gb, gn_sums, (__half*)out, rows_max,
@@ -961,6 +962,7 @@ extern "C" int w2v_conv0_noalloc(const float* audio, const long long* off, const
                                  int s0, int norm, const float* gw, const float* gb, void* out, long long rows_max,
                                  int max_frames, int* err, void* stream) {
     double* gn = nullptr;
+    if (C <= 0) return W2V_ERR_ARGS;
     if (norm == 1) {
         if (n_utt > kNoAllocMaxUtt || C > kNoAllocMaxChannels) return W2V_ERR_CAPACITY;
         const int rc = scratch_address(&gn);
