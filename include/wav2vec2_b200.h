@@ -89,6 +89,25 @@ int wav2vec2_b200_profile(struct wav2vec2_context * ctx, int enable);
 int wav2vec2_b200_profile_read(struct wav2vec2_context * ctx, const char ** names, double * ms,
                                long long * launches, double * flops, int cap);
 
+/* CTC prefix beam search on host logits [T, V] fp32, the decoder the
+ * reference runs for beam_size > 1 (wv2_ctc_beam_search, src/ops.h:151-251):
+ * writes the decoded token ids (runs collapsed, blank removed) to ids and
+ * returns their count; -1 on bad arguments (blank outside 0..V-1,
+ * beam_width < 1) or when more than cap ids result.  For host decoders that
+ * consume wav2vec2_b200_logits output; runs on the calling thread, no GPU. */
+int wav2vec2_b200_ctc_beam_search(const float * logits, int T, int V, int blank, int beam_width, int * ids,
+                                  int cap);
+
+/* Per-device load of the host batch path (wav2vec2_transcribe_batch,
+ * wav2vec2_b200_logits) since the last reset: busy_ms[i] = device time of
+ * device i's batches, each measured with CUDA events from before its first
+ * upload to after its last download; batches[i], samples[i] = batches and
+ * audio samples it processed.  Any output may be NULL; reset != 0 clears the
+ * totals after reading.  Returns the number of devices written (<= cap), -1
+ * on bad arguments.  No counterpart in the reference (single CPU). */
+int wav2vec2_b200_device_stats(struct wav2vec2_context * ctx, int reset, double * busy_ms,
+                               long long * batches, long long * samples, int cap);
+
 /* Kernel launches of the most recent forward on the first device. */
 long long wav2vec2_b200_launches_per_forward(const struct wav2vec2_context * ctx);
 

@@ -324,6 +324,25 @@ class RefOracle(_Base):
         return buf.value.decode()
 
 
+def ref_words_from_logits(ref: "RefOracle", logits):
+    """The reference's own greedy post-processing of given logits
+    (src/wav2vec2.cpp:497-503, 515-530): (transcript, [(word, t_start,
+    t_end)]) with times in seconds."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    T = lg.shape[0]
+    text = ctypes.create_string_buffer(1 << 16)
+    words = ctypes.create_string_buffer(1 << 16)
+    times = np.zeros(2 * (T + 1), np.float32)
+    L = RefOracle.lib()
+    L.w2vref_words_from_logits.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_char_p, ctypes.c_int,
+                                           ctypes.c_char_p, ctypes.c_int, _vp, ctypes.c_int]
+    n = L.w2vref_words_from_logits(ref.h, _p(lg), T, text, 1 << 16, words, 1 << 16, _p(times), T + 1)
+    if n < 0:
+        raise RuntimeError("reference word spans failed")
+    names = words.value.decode().split("\n") if n else []
+    return text.value.decode(), [(w, float(times[2 * i]), float(times[2 * i + 1])) for i, w in enumerate(names)]
+
+
 def ref_beam_search(logits, blank: int, beam: int) -> list[int]:
     lg = np.ascontiguousarray(logits, np.float32)
     T, V = lg.shape

@@ -163,6 +163,37 @@ int w2vref_greedy_spans(const float * logits, int T, int V, int * out, int cap_s
     return (int)s.size();
 }
 
+// The reference's greedy post-processing on given logits, exactly as its
+// public transcribe call runs it (wav2vec2.cpp:497-503, 515-530): greedy
+// spans, pad filter, ids_to_text and spans_to_words, with the word times
+// converted to seconds by the same float expression.  text receives the
+// transcript; words receives the words separated by '\n'; times[2i],
+// times[2i+1] = start, end of word i.  Returns the number of words, or -1.
+int w2vref_words_from_logits(wav2vec2_context * ctx, const float * logits, int T, char * text, int text_cap,
+                             char * words, int words_cap, float * times, int max_words) {
+    try {
+        const auto & m = ctx->model;
+        auto spans = wv2_ctc_greedy_spans(logits, T, m.vocab_size);
+        std::vector<int> ids;
+        for (const auto & sp : spans)
+            if (sp.token_id != m.pad_id) ids.push_back(sp.token_id);
+        std::string t = ids_to_text(ids, m.pad_id, m.vocab, m.word_delimiter);
+        auto ws = spans_to_words(spans, m.pad_id, m.vocab, m.word_delimiter);
+        if ((int)t.size() + 1 > text_cap || (int)ws.size() > max_words) return -1;
+        memcpy(text, t.c_str(), t.size() + 1);
+        std::string joined;
+        for (size_t i = 0; i < ws.size(); i++) {
+            if (i) joined += '\n';
+            joined += ws[i].word;
+            times[2 * i] = ws[i].t_start * (320.f / 16000.f);
+            times[2 * i + 1] = ws[i].t_end * (320.f / 16000.f);
+        }
+        if ((int)joined.size() + 1 > words_cap) return -1;
+        memcpy(words, joined.c_str(), joined.size() + 1);
+        return (int)ws.size();
+    } catch (const std::exception & e) { fprintf(stderr, "w2vref_words_from_logits: %s\n", e.what()); return -1; }
+}
+
 // Prefix beam search from logits (ops.h:162-251).
 int w2vref_beam_search(const float * logits, int T, int V, int blank, int beam, int * out, int cap) {
     auto ids = wv2_ctc_beam_search(logits, T, V, blank, beam);

@@ -54,6 +54,8 @@ SIGNATURES = {
     "wav2vec2_b200_profile": (_i, [_vp, _i]),
     "wav2vec2_b200_profile_read": (_i, [_vp, _vp, _vp, _vp, _vp, _i]),
     "wav2vec2_b200_launches_per_forward": (_ll, [_vp]),
+    "wav2vec2_b200_device_stats": (_i, [_vp, _i, _vp, _vp, _vp, _i]),
+    "wav2vec2_b200_ctc_beam_search": (_i, [_vp, _i, _i, _i, _i, _vp, _i]),
     "wav2vec2_b200_load_wav": (_i, [C.c_char_p, _i, _vp, _vp]),
     "wav2vec2_b200_free_samples": (None, [_vp]),
     # kernel layer (include/w2v_kernels.h)
@@ -108,6 +110,17 @@ def _ptr_array(arrs):
 
 class EngineError(RuntimeError):
     pass
+
+
+def ctc_beam_search(logits: np.ndarray, blank: int = 0, beam_width: int = 5) -> list[int]:
+    """Prefix beam search on host logits [T, V] (wav2vec2_b200_ctc_beam_search)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    T, V = lg.shape
+    out = np.zeros(max(T, 1), np.int32)
+    n = lib().wav2vec2_b200_ctc_beam_search(lg.ctypes.data, T, V, blank, beam_width, out.ctypes.data, out.size)
+    if n < 0:
+        raise EngineError(last_error())
+    return out[:n].tolist()
 
 
 def load_wav(path: str | Path, target_sr: int = 16000) -> np.ndarray:
@@ -234,6 +247,16 @@ class Model:
         k = lib().wav2vec2_b200_profile_read(self.h, C.cast(names, _vp), C.cast(ms, _vp), C.cast(nl, _vp),
                                              C.cast(fl, _vp), n)
         return {names[i].decode(): {"ms": ms[i], "launches": nl[i], "flops": fl[i]} for i in range(k)}
+
+    def device_stats(self, reset: bool = False) -> list[dict]:
+        """Per device: busy_ms (device time of its host batches), batches, samples."""
+        n = 64
+        ms = (C.c_double * n)()
+        nb = (C.c_longlong * n)()
+        ns = (C.c_longlong * n)()
+        k = lib().wav2vec2_b200_device_stats(self.h, 1 if reset else 0, C.cast(ms, _vp), C.cast(nb, _vp),
+                                             C.cast(ns, _vp), n)
+        return [{"busy_ms": ms[i], "batches": nb[i], "samples": ns[i]} for i in range(max(k, 0))]
 
     def launches_per_forward(self) -> int:
         return int(lib().wav2vec2_b200_launches_per_forward(self.h))

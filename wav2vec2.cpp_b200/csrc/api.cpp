@@ -28,6 +28,7 @@
 #include "engine.hpp"
 #include "shard.hpp"
 #include "audio.hpp"
+#include "beam.hpp"
 #include "wav2vec2_b200.h"
 
 using namespace w2v;
@@ -92,73 +93,6 @@ std::vector<Word> spans_to_words(const std::vector<Span>& spans, const ModelConf
     }
     flush();
     return words;
-}
-
-// ── prefix beam search (src/ops.h:151-251, Graves 2006, log domain) ─────────
-
-float log_sum_exp(float a, float b) {
-    if (a <= -1e29f) return b;
-    if (b <= -1e29f) return a;
-    const float mx = std::max(a, b);
-    return mx + log1pf(expf(std::min(a, b) - mx));
-}
-
-std::vector<int> beam_search(const float* logits, int T, int V, int blank, int width) {
-    constexpr float kNegInf = -1e30f;
-    struct State {
-        float pb = kNegInf, pnb = kNegInf;
-        float score() const { return log_sum_exp(pb, pnb); }
-    };
-    using Beams = std::map<std::vector<int>, State>;
-    Beams cur;
-    cur[{}].pb = 0.f;
-    std::vector<float> lp(V);
-    for (int t = 0; t < T; t++) {
-        const float* row = logits + (size_t)t * V;
-        const float mx = *std::max_element(row, row + V);
-        float z = 0.f;
-        for (int v = 0; v < V; v++) z += expf(row[v] - mx);
-        const float lz = mx + logf(z);
-        for (int v = 0; v < V; v++) lp[v] = row[v] - lz;
-        Beams next;
-        for (auto& [prefix, st] : cur) {
-            const int last = prefix.empty() ? -1 : prefix.back();
-            {
-                auto& ns = next[prefix];
-                ns.pb = log_sum_exp(ns.pb, log_sum_exp(st.pb, st.pnb) + lp[blank]);
-            }
-            for (int ch = 0; ch < V; ch++) {
-                if (ch == blank) continue;
-                if (ch == last) {
-                    auto& same = next[prefix];
-                    same.pnb = log_sum_exp(same.pnb, st.pnb + lp[ch]);
-                    auto ext = prefix;
-                    ext.push_back(ch);
-                    auto& ns = next[ext];
-                    ns.pnb = log_sum_exp(ns.pnb, st.pb + lp[ch]);
-                } else {
-                    auto ext = prefix;
-                    ext.push_back(ch);
-                    auto& ns = next[ext];
-                    ns.pnb = log_sum_exp(ns.pnb, log_sum_exp(st.pb, st.pnb) + lp[ch]);
-                }
-            }
-        }
-        cur.clear();
-        std::vector<std::pair<float, const std::vector<int>*>> ranked;
-        ranked.reserve(next.size());
-        for (auto& [k, st] : next) ranked.push_back({st.score(), &k});
-        std::sort(ranked.begin(), ranked.end(), [](const auto& a, const auto& b) { return a.first > b.first; });
-        const int keep = std::min((int)ranked.size(), width);
-        for (int i = 0; i < keep; i++) cur[*ranked[i].second] = next[*ranked[i].second];
-    }
-    const std::vector<int>* best = nullptr;
-    float bs = kNegInf;
-    for (auto& [k, st] : cur) {
-        const float s = st.score();
-        if (s > bs) { bs = s; best = &k; }
-    }
-    return best ? *best : std::vector<int>{};
 }
 
 // ── result assembly (src/wav2vec2.cpp:491-532) ──────────────────────────────
@@ -389,7 +323,7 @@ int wav2vec2_transcribe_batch(wav2vec2_context* ctx, wav2vec2_params params, con
                                     const int T = geo->T[j];
                                     const float* l = lg->data() + (size_t)geo->T_off[j] * c.vocab;
                                     const std::string text =
-                                        ids_to_text(beam_search(l, T, c.vocab, c.pad_id, params.beam_size), c);
+                                        ids_to_text(ctc_prefix_beam_search(l, T, c.vocab, c.pad_id, params.beam_size), c);
                                     results[u] = make_result(c, T, text, nullptr);
                                 });
                             }
@@ -553,6 +487,44 @@ int wav2vec2_b200_profile_read(wav2vec2_context* ctx, const char** names, double
                                double* flops, int cap) {
     if (!ctx) return -1;
     return ctx->engines[0]->profile_read(names, ms, launches, flops, cap);
+}
+
+int wav2vec2_b200_ctc_beam_search(const float* logits, int T, int V, int blank, int beam_width, int* ids,
+                                  int cap) {
+    if (T < 0 || V <= 0 || blank < 0 || blank >= V || beam_width < 1 || cap < 0 || (T > 0 && !logits) ||
+        (cap > 0 && !ids)) {
+        set_error("invalid arguments");
+        return -1;
+    }
+    try {
+        const auto r = ctc_prefix_beam_search(logits, T, V, blank, beam_width);
+        if ((int)r.size() > cap) {
+            set_error("output capacity too small");
+            return -1;
+        }
+        std::copy(r.begin(), r.end(), ids);
+        return (int)r.size();
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+int wav2vec2_b200_device_stats(wav2vec2_context* ctx, int reset, double* busy_ms, long long* batches,
+                               long long* samples, int cap) {
+    if (!ctx || cap < 0) return -1;
+    const int n = std::min<int>(cap, (int)ctx->engines.size());
+    for (int i = 0; i < (int)ctx->engines.size(); i++) {
+        double ms = 0;
+        long long nb = 0, ns = 0;
+        ctx->engines[i]->busy_stats(&ms, &nb, &ns, reset != 0);
+        if (i < n) {
+            if (busy_ms) busy_ms[i] = ms;
+            if (batches) batches[i] = nb;
+            if (samples) samples[i] = ns;
+        }
+    }
+    return n;
 }
 
 long long wav2vec2_b200_launches_per_forward(const wav2vec2_context* ctx) {

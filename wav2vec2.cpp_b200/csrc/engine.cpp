@@ -93,6 +93,17 @@ int Engine::profile_read(const char** names, double* ms, long long* launches, do
     return n;
 }
 
+void Engine::busy_stats(double* ms, long long* batches, long long* samples, bool reset) {
+    std::lock_guard<std::mutex> lk(busy_mu_);
+    if (ms) *ms = busy_ms_;
+    if (batches) *batches = busy_batches_;
+    if (samples) *samples = busy_samples_;
+    if (reset) {
+        busy_ms_ = 0.0;
+        busy_batches_ = busy_samples_ = 0;
+    }
+}
+
 // ── model configuration (src/wav2vec2.cpp:133-202) ──────────────────────────
 
 ModelConfig ModelConfig::from_gguf(const GgufFile& gf) {
@@ -172,6 +183,8 @@ Engine::Engine(const GgufFile& gf, const ModelConfig& cfg, int device) : cfg_(cf
     cuda_check(cudaEventCreateWithFlags(&meta_done_, cudaEventDisableTiming), "cudaEventCreate");
     cuda_check(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking), "cudaStreamCreate");
     for (auto& e : chunk_ev_) cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    cuda_check(cudaEventCreate(&busy0_), "cudaEventCreate");
+    cuda_check(cudaEventCreate(&busy1_), "cudaEventCreate");
     err_.ensure(sizeof(int));
     // Every transfer of the engine is ordered on its own (non-blocking) stream:
     // a legacy-stream cudaMemcpy from pageable memory may return before its DMA
@@ -201,6 +214,8 @@ Engine::~Engine() {
     prof_fold();
     for (auto e : ev_pool_) cudaEventDestroy(e);
     if (meta_done_) cudaEventDestroy(meta_done_);
+    if (busy0_) cudaEventDestroy(busy0_);
+    if (busy1_) cudaEventDestroy(busy1_);
     for (auto e : chunk_ev_)
         if (e) cudaEventDestroy(e);
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
@@ -693,6 +708,9 @@ void Engine::run_host(const std::vector<const float*>& audio, const std::vector<
         pinned = cudaPointerGetAttributes(&at, audio[u]) == cudaSuccess && at.type == cudaMemoryTypeHost;
     }
     cudaGetLastError();   // a pageable pointer may leave an error from the query
+    // device span of this batch: from before its first upload (copy stream)
+    // to after its last download (compute stream)
+    cuda_check(cudaEventRecord(busy0_, copy_stream_), "busy event");
     if (pinned && fwd_begin(g, stream_)) {
         for (int k = 0; k < nch; k++) {
             for (int u = cu[k]; u < cu[k + 1]; u++)
@@ -754,7 +772,18 @@ void Engine::run_host(const std::vector<const float*>& audio, const std::vector<
     if (ns_bytes)
         cuda_check(cudaMemcpyAsync(h_out_ + 16 + sp_bytes, nspans_.p, ns_bytes, cudaMemcpyDeviceToHost, stream_),
                    "spans download");
+    cuda_check(cudaEventRecord(busy1_, stream_), "busy event");
     cuda_check(cudaStreamSynchronize(stream_), "forward");
+    {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, busy0_, busy1_) == cudaSuccess) {
+            std::lock_guard<std::mutex> lk(busy_mu_);
+            busy_ms_ += ms;
+            busy_batches_ += 1;
+            busy_samples_ += (long long)total;
+        }
+        cudaGetLastError();
+    }
     int e = 0;
     memcpy(&e, h_out_, sizeof(int));
     if (e) {

@@ -11,6 +11,7 @@
 #include <cstdint>
 #include <memory>
 #include <string>
+#include <mutex>
 #include <vector>
 
 #include "gguf.hpp"
@@ -102,6 +103,10 @@ public:
     // returns the number of categories written (<= cap).
     int profile_read(const char** names, double* ms, long long* launches, double* flops, int cap);
     long long launches_last_forward() const { return launches_last_; }
+    // Host batches run since the last reset: device time from the first
+    // upload to the last download of each batch (CUDA events), batch and
+    // sample counts.
+    void busy_stats(double* ms, long long* batches, long long* samples, bool reset);
 
 private:
     void load(const GgufFile& gf);
@@ -163,6 +168,10 @@ private:
     static constexpr int kMaxChunks = 4;
     cudaStream_t copy_stream_ = nullptr;
     cudaEvent_t chunk_ev_[kMaxChunks] = {};
+    cudaEvent_t busy0_ = nullptr, busy1_ = nullptr;
+    std::mutex busy_mu_;
+    double busy_ms_ = 0.0;
+    long long busy_batches_ = 0, busy_samples_ = 0;
 
     // device pointers into meta_
     long long* d_audio_off_ = nullptr;
