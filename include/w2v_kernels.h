@@ -70,6 +70,39 @@ int w2v_gemm_f16_ln_resid(const void* A, long long a_cin, int a_taps, int a_stri
                           const float* resid, long long ldr, const float* ln_stats, const float* ln_w,
                           const float* ln_b, int block_n, int* err, void* stream);
 
+/* Dequant-fused tcgen05 GEMM on quantised weights: C = epi(A . W^T) with W
+ * the [N, K] rows of a GGUF Q8_0 (gguf_type 8) or Q4_0 (gguf_type 2) linear
+ * (scripts/convert_to_gguf.py:63-97), kept in the planes w2v_repack_q
+ * writes: Bq the codes, Bs the fp16 scales [K/32][ld_s] (ld_s >= N, a
+ * multiple of 8).  Converter warps expand each 64-deep k-block of W to fp16
+ * straight into tensor memory (w = d*q rounded once: the values
+ * w2v_dequant_f16 gives), where the MMA reads it as its A operand.  Replaces
+ * ggml_mul_mat on quantised weights (GgmlScratch::linear,
+ * src/ggml_backend.h:78-120).  A: fp16 [M, K] activation rows (K % 64 == 0);
+ * C, bias, resid and the epilogues as w2v_gemm_f16 (not
+ * W2V_EPI_F32_RESID_LN: w2v_gemm_q_ln_resid).  block_n: 0 = automatic,
+ * 128/192 = one CTA per 128 weight rows x block_n activation rows,
+ * -128/-192 = a CTA pair per 256 weight rows x -block_n activation rows. */
+int w2v_gemm_q(const void* A, long long K, long long M, const void* Bq, const void* Bs, long long ld_s,
+               int gguf_type, int N, void* C, long long ldc, const float* bias, const float* resid,
+               long long ldr, int epilogue, int block_n, int* err, void* stream);
+
+/* w2v_gemm_q with the W2V_EPI_F32_RESID_LN epilogue (see w2v_gemm_f16_ln_resid). */
+int w2v_gemm_q_ln_resid(const void* A, long long K, long long M, const void* Bq, const void* Bs,
+                        long long ld_s, int gguf_type, int N, void* C, long long ldc, const float* bias,
+                        const float* resid, long long ldr, const float* ln_stats, const float* ln_w,
+                        const float* ln_b, int block_n, int* err, void* stream);
+
+/* GGUF Q8_0 / Q4_0 blocks of weight rows [n_rows, K] (K % 64 == 0; raw
+ * bytes as stored in the file, the way src/ggml_backend.h:43-50 keeps them)
+ * -> the planes of w2v_gemm_q: codes = [n_rows][K] int8 (Q8_0) or
+ * [n_rows][K/2] bytes of 4-bit codes (Q4_0), 16-byte aligned; scales[j*ld_s
+ * + n] = fp16 scale of row n's j-th block of 32.  Rows may be written into a
+ * larger plane (stacked Q/K/V): pass codes and scales offset to the first row
+ * / column. */
+int w2v_repack_q(const void* raw, int gguf_type, long long n_rows, long long K, void* codes, void* scales,
+                 long long ld_s, void* stream);
+
 /* Failure-detection self-test: launches a kernel whose bounded mbarrier wait
  * (the same wait the GEMM pipeline uses) is never satisfied; after limit_ms
  * (1..2000) it writes the timeout code (1) to *err and returns without

@@ -108,6 +108,14 @@ int wav2vec2_b200_ctc_beam_search(const float * logits, int T, int V, int blank,
 int wav2vec2_b200_device_stats(struct wav2vec2_context * ctx, int reset, double * busy_ms,
                                long long * batches, long long * samples, int cap);
 
+/* Device bytes that the first device holds for the linear layers (feature
+ * projection, encoder Q/K/V/out/FFN, CTC head): Q8_0 / Q4_0 linears stay
+ * quantised (code plane + fp16 scale plane, expanded inside the GEMM), F16 /
+ * F32 ones are fp16 rows.  The environment variable W2V_B200_EXPAND_WEIGHTS=1,
+ * read when a context is created, expands every linear to fp16 rows instead.
+ * -1 on a NULL context. */
+long long wav2vec2_b200_linear_weight_bytes(const struct wav2vec2_context * ctx);
+
 /* Kernel launches of the most recent forward on the first device. */
 long long wav2vec2_b200_launches_per_forward(const struct wav2vec2_context * ctx);
 

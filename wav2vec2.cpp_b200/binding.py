@@ -56,6 +56,7 @@ SIGNATURES = {
     "wav2vec2_b200_launches_per_forward": (_ll, [_vp]),
     "wav2vec2_b200_device_stats": (_i, [_vp, _i, _vp, _vp, _vp, _i]),
     "wav2vec2_b200_ctc_beam_search": (_i, [_vp, _i, _i, _i, _i, _vp, _i]),
+    "wav2vec2_b200_linear_weight_bytes": (_ll, [_vp]),
     "wav2vec2_b200_load_wav": (_i, [C.c_char_p, _i, _vp, _vp]),
     "wav2vec2_b200_free_samples": (None, [_vp]),
     # kernel layer (include/w2v_kernels.h)
@@ -63,6 +64,10 @@ SIGNATURES = {
                           _i, _vp, _vp]),
     "w2v_gemm_f16_ln_resid": (_i, [_vp, _ll, _i, _i, _ll, _ll, _ll, _ll, _vp, _i, _vp, _ll, _ll, _i, _vp, _vp,
                                    _ll, _vp, _vp, _vp, _i, _vp, _vp]),
+    "w2v_gemm_q": (_i, [_vp, _ll, _ll, _vp, _vp, _ll, _i, _i, _vp, _ll, _vp, _vp, _ll, _i, _i, _vp, _vp]),
+    "w2v_gemm_q_ln_resid": (_i, [_vp, _ll, _ll, _vp, _vp, _ll, _i, _i, _vp, _ll, _vp, _vp, _ll, _vp, _vp, _vp, _i,
+                                 _vp, _vp]),
+    "w2v_repack_q": (_i, [_vp, _i, _ll, _ll, _vp, _vp, _ll, _vp]),
     "w2v_layer_norm_stats": (_i, [_vp, _ll, _i, _vp, _vp, _vp, _vp, _vp]),
     "w2v_selftest_wait_timeout": (_i, [_vp, _i, _vp]),
     "w2v_dequant_f16": (_i, [_vp, _i, _ll, _ll, _vp, _vp]),
@@ -258,6 +263,9 @@ class Model:
                                              C.cast(ns, _vp), n)
         return [{"busy_ms": ms[i], "batches": nb[i], "samples": ns[i]} for i in range(max(k, 0))]
 
+    def linear_weight_bytes(self) -> int:
+        return int(lib().wav2vec2_b200_linear_weight_bytes(self.h))
+
     def launches_per_forward(self) -> int:
         return int(lib().wav2vec2_b200_launches_per_forward(self.h))
 
@@ -291,6 +299,24 @@ class kernels:
                                                   a_batch_stride, B, N, Cp, ldc, c_batch_rows, m_valid,
                                                   bias or None, resid, ldr, ln_stats, ln_w, ln_b, block_n,
                                                   err or None, stream or None), "w2v_gemm_f16_ln_resid")
+
+    @staticmethod
+    def gemm_q(A, K, M, Bq, Bs, ld_s, gguf_type, N, Cp, ldc, bias=0, resid=0, ldr=0, epilogue=0, block_n=0, err=0,
+               stream=0):
+        kernels.check(lib().w2v_gemm_q(A, K, M, Bq, Bs, ld_s, gguf_type, N, Cp, ldc, bias or None, resid or None,
+                                       ldr, epilogue, block_n, err or None, stream or None), "w2v_gemm_q")
+
+    @staticmethod
+    def gemm_q_ln_resid(A, K, M, Bq, Bs, ld_s, gguf_type, N, Cp, ldc, bias, resid, ldr, ln_stats, ln_w, ln_b,
+                        block_n=0, err=0, stream=0):
+        kernels.check(lib().w2v_gemm_q_ln_resid(A, K, M, Bq, Bs, ld_s, gguf_type, N, Cp, ldc, bias or None, resid,
+                                                ldr, ln_stats, ln_w, ln_b, block_n, err or None, stream or None),
+                      "w2v_gemm_q_ln_resid")
+
+    @staticmethod
+    def repack_q(raw, gguf_type, n_rows, K, codes, scales, ld_s, stream=0):
+        kernels.check(lib().w2v_repack_q(raw, gguf_type, n_rows, K, codes, scales, ld_s, stream or None),
+                      "w2v_repack_q")
 
     @staticmethod
     def layer_norm_stats(inp, M, D, w, b, out16, stats, stream=0):

@@ -527,6 +527,10 @@ int wav2vec2_b200_device_stats(wav2vec2_context* ctx, int reset, double* busy_ms
     return n;
 }
 
+long long wav2vec2_b200_linear_weight_bytes(const wav2vec2_context* ctx) {
+    return ctx && !ctx->engines.empty() ? (long long)ctx->engines[0]->linear_weight_bytes() : -1;
+}
+
 long long wav2vec2_b200_launches_per_forward(const wav2vec2_context* ctx) {
     return ctx ? ctx->engines[0]->launches_last_forward() : 0;
 }

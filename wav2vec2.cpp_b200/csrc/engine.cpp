@@ -185,6 +185,7 @@ Engine::Engine(const GgufFile& gf, const ModelConfig& cfg, int device) : cfg_(cf
     for (auto& e : chunk_ev_) cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
     cuda_check(cudaEventCreate(&busy0_), "cudaEventCreate");
     cuda_check(cudaEventCreate(&busy1_), "cudaEventCreate");
+    if (const char* e = getenv("W2V_B200_EXPAND_WEIGHTS")) expand_weights_ = atoi(e) != 0;
     err_.ensure(sizeof(int));
     // Every transfer of the engine is ordered on its own (non-blocking) stream:
     // a legacy-stream cudaMemcpy from pageable memory may return before its DMA
@@ -199,14 +200,16 @@ Engine::~Engine() {
     if (stream_) cudaStreamSynchronize(stream_);
     if (copy_stream_) cudaStreamSynchronize(copy_stream_);
     auto rel = [](DevBuf& b) { b.release(); };
-    for (DevBuf* b : {&conv0_w_, &conv0_b_, &proj_lnw_, &proj_lnb_, &proj_w_, &proj_b_, &pos_w_, &pos_b_, &enc_lnw_,
-                      &enc_lnb_, &lm_w_, &lm_b_, &audio_stage_, &meta_, &stats_, &gn_, &actA_, &actB_, &feat_,
+    for (DevBuf* b : {&conv0_w_, &conv0_b_, &proj_lnw_, &proj_lnb_, &proj_w_.w, &proj_w_.s, &proj_b_, &pos_w_, &pos_b_,
+                      &enc_lnw_, &enc_lnb_, &lm_w_.w, &lm_w_.s, &lm_b_, &audio_stage_, &meta_, &stats_, &gn_, &actA_,
+                      &actB_, &feat_,
                       &pbuf_, &x_, &xh_, &qkv_, &attn_, &hbuf_, &ybuf_, &lnstats_, &logits_, &ids_, &spans_, &nspans_, &err_})
         rel(*b);
     for (auto* v : {&conv_w_, &conv_b_, &conv_gw_, &conv_gb_})
         for (auto& b : *v) rel(b);
     for (auto& L : layers_)
-        for (DevBuf* b : {&L.wqkv, &L.bqkv, &L.wo, &L.bo, &L.w1, &L.b1, &L.w2, &L.b2, &L.ln1w, &L.ln1b, &L.ln2w,
+        for (DevBuf* b : {&L.qkv.w, &L.qkv.s, &L.bqkv, &L.o.w, &L.o.s, &L.bo, &L.fc1.w, &L.fc1.s, &L.b1, &L.fc2.w,
+                          &L.fc2.s, &L.b2, &L.ln1w, &L.ln1b, &L.ln2w,
                           &L.ln2b})
             rel(*b);
     if (h_audio_) cudaFreeHost(h_audio_);
@@ -245,23 +248,77 @@ static void upload_f16(DevBuf& d, const std::vector<float>& v, cudaStream_t st) 
     tmp.release();
 }
 
-void Engine::upload_linear(const GgufFile& gf, const std::string& name, int N, int K, DevBuf& w,
-                           size_t row_offset) {
-    const auto& t = gf.tensor(name + ".weight");
-    // GGUF dims are innermost first: [K, N] (src/wav2vec2.cpp:116-125)
-    if (t.shape.size() < 2 || (int)t.shape[0] != K || (int)t.shape[1] != N)
-        throw std::runtime_error("tensor shape mismatch: " + name + ".weight");
-    if (t.type != GT_F32 && t.type != GT_F16 && t.type != GT_Q8_0 && t.type != GT_Q4_0)
-        throw std::runtime_error("unsupported weight type " + std::to_string(t.type) + " for " + name);
-    if (t.nbytes != gguf_nbytes(t.type, (uint64_t)N * K))
-        throw std::runtime_error("tensor size mismatch: " + name + ".weight");
-    DevBuf raw;
-    raw.ensure(t.nbytes);
-    cuda_check(cudaMemcpyAsync(raw.p, t.data, t.nbytes, cudaMemcpyHostToDevice, stream_), "weight upload");
-    w2v_check(w2v_dequant_f16(raw.p, (int)t.type, N, K, static_cast<uint16_t*>(w.p) + row_offset * K, stream_),
-              "weight expansion");
-    cuda_check(cudaStreamSynchronize(stream_), "weight expansion");
-    raw.release();
+void Engine::upload_linears(const GgufFile& gf, const std::vector<std::string>& names, const std::vector<int>& Ns,
+                            int K, LinearW& L) {
+    int N = 0, type = -1;
+    bool same = true;
+    for (size_t i = 0; i < names.size(); i++) {
+        const auto& t = gf.tensor(names[i] + ".weight");
+        // GGUF dims are innermost first: [K, N] (src/wav2vec2.cpp:116-125)
+        if (t.shape.size() < 2 || (int)t.shape[0] != K || (int)t.shape[1] != Ns[i])
+            throw std::runtime_error("tensor shape mismatch: " + names[i] + ".weight");
+        if (t.type != GT_F32 && t.type != GT_F16 && t.type != GT_Q8_0 && t.type != GT_Q4_0)
+            throw std::runtime_error("unsupported weight type " + std::to_string(t.type) + " for " + names[i]);
+        if (t.nbytes != gguf_nbytes(t.type, (uint64_t)Ns[i] * K))
+            throw std::runtime_error("tensor size mismatch: " + names[i] + ".weight");
+        same = same && (type < 0 || (int)t.type == type);
+        type = (int)t.type;
+        N += Ns[i];
+    }
+    const bool quant = same && (type == GT_Q8_0 || type == GT_Q4_0) && K % 64 == 0 && !expand_weights_;
+    L.N = N;
+    L.K = K;
+    L.gguf_type = quant ? type : (int)GT_F16;
+    // codes [N][K] int8 or [N][K/2] 4-bit; scales [K/32][N'] fp16 with N' = N rounded up to 8 (16-byte rows)
+    const size_t row_bytes = type == GT_Q8_0 ? (size_t)K : (size_t)K / 2;
+    const size_t ld_s = ((size_t)N + 7) / 8 * 8;
+    if (quant) {
+        L.w.ensure((size_t)N * row_bytes);
+        L.s.ensure((size_t)(K / 32) * ld_s * 2);
+    } else {
+        L.w.ensure((size_t)N * K * 2);
+    }
+    size_t row0 = 0;
+    for (size_t i = 0; i < names.size(); i++) {
+        const auto& t = gf.tensor(names[i] + ".weight");
+        DevBuf raw;
+        raw.ensure(t.nbytes);
+        cuda_check(cudaMemcpyAsync(raw.p, t.data, t.nbytes, cudaMemcpyHostToDevice, stream_), "weight upload");
+        if (quant)
+            w2v_check(w2v_repack_q(raw.p, (int)t.type, Ns[i], K, L.w.as<uint8_t>() + row0 * row_bytes,
+                                   L.s.as<uint16_t>() + row0, (long long)ld_s, stream_),
+                      "weight repack");
+        else
+            w2v_check(w2v_dequant_f16(raw.p, (int)t.type, Ns[i], K, L.w.as<uint16_t>() + row0 * K, stream_),
+                      "weight expansion");
+        cuda_check(cudaStreamSynchronize(stream_), "weight upload");
+        raw.release();
+        row0 += (size_t)Ns[i];
+    }
+}
+
+int Engine::gemm_linear(const void* A, long long M, const LinearW& L, void* C, long long ldc, const float* bias,
+                        const float* resid, int epilogue, int block_n, const float* ln_stats, const float* ln_w,
+                        const float* ln_b, cudaStream_t st) {
+    int* err = err_.as<int>();
+    if (L.gguf_type == GT_F16) {
+        if (epilogue == W2V_EPI_F32_RESID_LN)
+            return w2v_gemm_f16_ln_resid(A, L.K, 1, 1, L.K, M, 1, M * L.K, L.w.p, L.N, C, ldc, M, (int)M, bias, resid,
+                                         ldc, ln_stats, ln_w, ln_b, block_n, err, st);
+        return w2v_gemm_f16(A, L.K, 1, 1, L.K, M, 1, M * L.K, L.w.p, L.N, C, ldc, M, (int)M, bias, resid, ldc,
+                            epilogue, block_n, err, st);
+    }
+    const long long ld_s = (L.N + 7) / 8 * 8;
+    if (epilogue == W2V_EPI_F32_RESID_LN)
+        return w2v_gemm_q_ln_resid(A, L.K, M, L.w.p, L.s.p, ld_s, L.gguf_type, L.N, C, ldc, bias, resid, ldc, ln_stats,
+                                   ln_w, ln_b, 0, err, st);
+    return w2v_gemm_q(A, L.K, M, L.w.p, L.s.p, ld_s, L.gguf_type, L.N, C, ldc, bias, resid, ldc, epilogue, 0, err, st);
+}
+
+size_t Engine::linear_weight_bytes() const {
+    size_t n = proj_w_.bytes() + lm_w_.bytes();
+    for (const auto& L : layers_) n += L.qkv.bytes() + L.o.bytes() + L.fc1.bytes() + L.fc2.bytes();
+    return n;
 }
 
 void Engine::load(const GgufFile& gf) {
@@ -293,8 +350,7 @@ void Engine::load(const GgufFile& gf) {
     // feature projection (src/wav2vec2.cpp:205-208)
     upload_floats(proj_lnw_, floats_sized(gf, "feature_projection.layer_norm.weight", C), stream_);
     upload_floats(proj_lnb_, floats_sized(gf, "feature_projection.layer_norm.bias", C), stream_);
-    proj_w_.ensure((size_t)H * C * 2);
-    upload_linear(gf, "feature_projection.projection", H, C, proj_w_);
+    upload_linears(gf, {"feature_projection.projection"}, {H}, C, proj_w_);
     upload_floats(proj_b_, floats_sized(gf, "feature_projection.projection.bias", H), stream_);
     // positional conv [H][Cg][Kp] (src/wav2vec2.cpp:211-212) -> per tap, 8-channel
     // core-matrix blocks: [G][Kp][Cg/8 (ci chunk)][Cg (co)][8 (ci)]
@@ -318,24 +374,19 @@ void Engine::load(const GgufFile& gf) {
     for (int l = 0; l < c.n_layers; l++) {
         auto& L = layers_[l];
         const std::string p = "encoder.layers." + std::to_string(l);
-        L.wqkv.ensure((size_t)3 * H * H * 2);
-        upload_linear(gf, p + ".attention.q_proj", H, H, L.wqkv, 0);
-        upload_linear(gf, p + ".attention.k_proj", H, H, L.wqkv, (size_t)H);
-        upload_linear(gf, p + ".attention.v_proj", H, H, L.wqkv, (size_t)2 * H);
+        upload_linears(gf, {p + ".attention.q_proj", p + ".attention.k_proj", p + ".attention.v_proj"}, {H, H, H}, H,
+                       L.qkv);
         std::vector<float> bq = floats_sized(gf, p + ".attention.q_proj.bias", H);
         auto bk = floats_sized(gf, p + ".attention.k_proj.bias", H);
         auto bv = floats_sized(gf, p + ".attention.v_proj.bias", H);
         bq.insert(bq.end(), bk.begin(), bk.end());
         bq.insert(bq.end(), bv.begin(), bv.end());
         upload_floats(L.bqkv, bq, stream_);
-        L.wo.ensure((size_t)H * H * 2);
-        upload_linear(gf, p + ".attention.out_proj", H, H, L.wo);
+        upload_linears(gf, {p + ".attention.out_proj"}, {H}, H, L.o);
         upload_floats(L.bo, floats_sized(gf, p + ".attention.out_proj.bias", H), stream_);
-        L.w1.ensure((size_t)F * H * 2);
-        upload_linear(gf, p + ".feed_forward.intermediate_dense", F, H, L.w1);
+        upload_linears(gf, {p + ".feed_forward.intermediate_dense"}, {F}, H, L.fc1);
         upload_floats(L.b1, floats_sized(gf, p + ".feed_forward.intermediate_dense.bias", F), stream_);
-        L.w2.ensure((size_t)H * F * 2);
-        upload_linear(gf, p + ".feed_forward.output_dense", H, F, L.w2);
+        upload_linears(gf, {p + ".feed_forward.output_dense"}, {H}, F, L.fc2);
         upload_floats(L.b2, floats_sized(gf, p + ".feed_forward.output_dense.bias", H), stream_);
         upload_floats(L.ln1w, floats_sized(gf, p + ".layer_norm.weight", H), stream_);
         upload_floats(L.ln1b, floats_sized(gf, p + ".layer_norm.bias", H), stream_);
@@ -343,8 +394,7 @@ void Engine::load(const GgufFile& gf) {
         upload_floats(L.ln2b, floats_sized(gf, p + ".final_layer_norm.bias", H), stream_);
     }
     // CTC head (src/wav2vec2.cpp:245-246)
-    lm_w_.ensure((size_t)V * H * 2);
-    upload_linear(gf, "lm_head", V, H, lm_w_);
+    upload_linears(gf, {"lm_head"}, {V}, H, lm_w_);
     upload_floats(lm_b_, floats_sized(gf, "lm_head.bias", V), stream_);
 }
 
@@ -520,21 +570,16 @@ void Engine::fwd_extract(const float* d_audio, const BatchGeom& g, int u0, int u
 
 void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, float* dbg_stages) {
     const ModelConfig& c = cfg_;
-    const int B = g.n_utt, C = c.conv_dim, H = c.hidden, F = c.ffn, V = c.vocab;
+    const int B = g.n_utt, C = c.conv_dim, H = c.hidden, V = c.vocab;
     int* err = err_.as<int>();
     const long long M = g.M;
-    auto gemm = [&](int cat, const void* A, long long cin, int taps, int stride, long long row_stride,
-                    long long rows_in, long long batches, long long batch_stride, const void* W, int N, void* out,
-                    long long ldc, long long c_batch_rows, int m_valid, const void* bias, const float* resid, int epi,
-                    double flops, int bn = 0) {
-        launch(cat, flops, st, "gemm", [&] {
-            return w2v_gemm_f16(A, cin, taps, stride, row_stride, rows_in, batches, batch_stride, W, N, out, ldc,
-                                c_batch_rows, m_valid, static_cast<const float*>(bias), resid, ldc, epi, bn, err, st);
-        });
-    };
-    auto plain_gemm = [&](int cat, const void* A, int K, const void* W, int N, void* out, const void* bias,
+    (void)err;
+    // one linear over the packed rows: fp16 or dequant-fused GEMM by the weights' format
+    auto plain_gemm = [&](int cat, const void* A, const LinearW& W, void* out, const DevBuf& bias,
                           const float* resid, int epi, int bn = 0) {
-        gemm(cat, A, K, 1, 1, K, M, 1, M * K, W, N, out, N, M, (int)M, bias, resid, epi, 2.0 * M * N * K, bn);
+        launch(cat, 2.0 * M * W.N * W.K, st, "gemm", [&] {
+            return gemm_linear(A, M, W, out, W.N, bias.as<float>(), resid, epi, bn, nullptr, nullptr, nullptr, st);
+        });
     };
     auto dbg_copy = [&](int block, const float* src) {
         if (!dbg_stages) return;
@@ -557,7 +602,7 @@ void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, fl
         return w2v_layer_norm(cur, 1, C, g.R[c.n_conv - 1], d_T_, d_T_off_, B, 0, C, proj_lnw_.as<float>(),
                               proj_lnb_.as<float>(), 0, nullptr, feat_.p, C, st);
     });
-    plain_gemm(P_GEMM_PROJ, feat_.p, C, proj_w_.p, H, pbuf_.p, proj_b_.p, nullptr, W2V_EPI_F32);
+    plain_gemm(P_GEMM_PROJ, feat_.p, proj_w_, pbuf_.p, proj_b_, nullptr, W2V_EPI_F32);
     dbg_copy(0, pbuf_.as<float>());
     // 4. positional conv embedding + residual (src/wav2vec2.cpp:349-356)
     float* x = x_.as<float>();
@@ -591,11 +636,11 @@ void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, fl
                 return w2v_layer_norm_stats(x, M, H, w.as<float>(), b.as<float>(), xh_.p, lst, st);
             });
         };
-        auto resid_ln_gemm = [&](const void* A, int K, const DevBuf& W, const DevBuf& bias, const DevBuf& lw,
+        auto resid_ln_gemm = [&](const void* A, const LinearW& W, const DevBuf& bias, const DevBuf& lw,
                                  const DevBuf& lb) {
-            launch(P_GEMM_ENC, 2.0 * M * H * K, st, "gemm", [&] {
-                return w2v_gemm_f16_ln_resid(A, K, 1, 1, K, M, 1, M * K, W.p, H, x, H, M, (int)M,
-                                             bias.as<float>(), x, H, lst, lw.as<float>(), lb.as<float>(), 0, err, st);
+            launch(P_GEMM_ENC, 2.0 * M * W.N * W.K, st, "gemm", [&] {
+                return gemm_linear(A, M, W, x, H, bias.as<float>(), x, W2V_EPI_F32_RESID_LN, 0, lst, lw.as<float>(),
+                                   lb.as<float>(), st);
             });
         };
         auto dbg_norm = [&](int block, const DevBuf& lw, const DevBuf& lb) {   // debug: materialise LN(x)
@@ -609,12 +654,12 @@ void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, fl
         const DevBuf* pb = &enc_lnb_;
         for (int l = 0; l < c.n_layers; l++) {
             const auto& L = layers_[l];
-            plain_gemm(P_GEMM_ENC, xh_.p, H, L.wqkv.p, 3 * H, qkv_.p, L.bqkv.p, nullptr, W2V_EPI_F16);
+            plain_gemm(P_GEMM_ENC, xh_.p, L.qkv, qkv_.p, L.bqkv, nullptr, W2V_EPI_F16);
             attention();
-            resid_ln_gemm(attn_.p, H, L.wo, L.bo, *pw, *pb);
+            resid_ln_gemm(attn_.p, L.o, L.bo, *pw, *pb);
             ln_stats(L.ln1w, L.ln1b);
-            plain_gemm(P_GEMM_ENC, xh_.p, H, L.w1.p, F, hbuf_.p, L.b1.p, nullptr, W2V_EPI_F16_GELU);
-            resid_ln_gemm(hbuf_.p, F, L.w2, L.b2, L.ln1w, L.ln1b);
+            plain_gemm(P_GEMM_ENC, xh_.p, L.fc1, hbuf_.p, L.b1, nullptr, W2V_EPI_F16_GELU);
+            resid_ln_gemm(hbuf_.p, L.fc2, L.b2, L.ln1w, L.ln1b);
             ln_stats(L.ln2w, L.ln2b);
             pw = &L.ln2w;
             pb = &L.ln2b;
@@ -626,19 +671,19 @@ void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, fl
         for (int l = 0; l < c.n_layers; l++) {
             const auto& L = layers_[l];
             ln_rows(x, nullptr, xh_.p, L.ln1w, L.ln1b);
-            plain_gemm(P_GEMM_ENC, xh_.p, H, L.wqkv.p, 3 * H, qkv_.p, L.bqkv.p, nullptr, W2V_EPI_F16);
+            plain_gemm(P_GEMM_ENC, xh_.p, L.qkv, qkv_.p, L.bqkv, nullptr, W2V_EPI_F16);
             attention();
-            plain_gemm(P_GEMM_ENC, attn_.p, H, L.wo.p, H, x, L.bo.p, x, W2V_EPI_F32_RESID);
+            plain_gemm(P_GEMM_ENC, attn_.p, L.o, x, L.bo, x, W2V_EPI_F32_RESID);
             ln_rows(x, nullptr, xh_.p, L.ln2w, L.ln2b);
-            plain_gemm(P_GEMM_ENC, xh_.p, H, L.w1.p, F, hbuf_.p, L.b1.p, nullptr, W2V_EPI_F16_GELU);
-            plain_gemm(P_GEMM_ENC, hbuf_.p, F, L.w2.p, H, x, L.b2.p, x, W2V_EPI_F32_RESID);
+            plain_gemm(P_GEMM_ENC, xh_.p, L.fc1, hbuf_.p, L.b1, nullptr, W2V_EPI_F16_GELU);
+            plain_gemm(P_GEMM_ENC, hbuf_.p, L.fc2, x, L.b2, x, W2V_EPI_F32_RESID);
             if (l == c.n_layers - 1) ln_rows(x, x, xh_.p, enc_lnw_, enc_lnb_);
             dbg_copy(2 + l, x);
         }
         if (c.n_layers == 0) ln_rows(x, x, xh_.p, enc_lnw_, enc_lnb_);
     }
     // 5. CTC head + greedy decode (src/wav2vec2.cpp:489, 498-503)
-    plain_gemm(P_GEMM_LM, xh_.p, H, lm_w_.p, V, logits_.p, lm_b_.p, nullptr, W2V_EPI_F32, 64);
+    plain_gemm(P_GEMM_LM, xh_.p, lm_w_, logits_.p, lm_b_, nullptr, W2V_EPI_F32, lm_w_.gguf_type == GT_F16 ? 64 : 0);
     launch(P_CTC, 0.0, st, "ctc_greedy", [&] {
         return w2v_ctc_greedy(logits_.as<float>(), d_T_off_, d_T_, B, V, ids_.as<int>(), spans_.as<int>(),
                               nspans_.as<int>(), g.T_max, st);

@@ -42,8 +42,20 @@ struct DevBuf {
     template <typename T> T* as() const { return static_cast<T*>(p); }
 };
 
+// One linear's weights on the device: fp16 rows [N, K] (gguf_type 1), or the
+// GGUF Q8_0 (8) / Q4_0 (2) blocks repacked into a code plane and a scale
+// plane [K/32][N] that the dequant-fused GEMM reads (w2v_gemm_q).
+struct LinearW {
+    DevBuf w;             // fp16 rows, or the codes
+    DevBuf s;             // quantised: fp16 scales
+    int gguf_type = 1;
+    int N = 0, K = 0;
+    size_t bytes() const { return w.n + s.n; }
+};
+
 struct LayerWeights {
-    DevBuf wqkv, bqkv, wo, bo, w1, b1, w2, b2, ln1w, ln1b, ln2w, ln2b;
+    LinearW qkv, o, fc1, fc2;
+    DevBuf bqkv, bo, b1, b2, ln1w, ln1b, ln2w, ln2b;
 };
 
 // Everything one forward pass needs per batch.
@@ -103,6 +115,8 @@ public:
     // returns the number of categories written (<= cap).
     int profile_read(const char** names, double* ms, long long* launches, double* flops, int cap);
     long long launches_last_forward() const { return launches_last_; }
+    // Device bytes of the linear weights (codes + scales, or fp16 rows).
+    size_t linear_weight_bytes() const;
     // Host batches run since the last reset: device time from the first
     // upload to the last download of each batch (CUDA events), batch and
     // sample counts.
@@ -110,8 +124,15 @@ public:
 
 private:
     void load(const GgufFile& gf);
-    void upload_linear(const GgufFile& gf, const std::string& name, int N, int K, DevBuf& w,
-                       size_t row_offset = 0);
+    // Weight rows of GGUF linears `names` (each [N_i, K]) stacked into one
+    // linear: kept quantised when they share a Q8_0 / Q4_0 type (unless the
+    // engine expands every weight to fp16), else expanded to fp16.
+    void upload_linears(const GgufFile& gf, const std::vector<std::string>& names, const std::vector<int>& Ns, int K,
+                        LinearW& L);
+    // One GEMM over packed encoder rows [M, K] with linear L's weights.
+    int gemm_linear(const void* A, long long M, const LinearW& L, void* C, long long ldc, const float* bias,
+                    const float* resid, int epilogue, int block_n, const float* ln_stats, const float* ln_w,
+                    const float* ln_b, cudaStream_t st);
     void ensure_workspace(const BatchGeom& g);
     void upload_meta(const BatchGeom& g, cudaStream_t st);
     // The forward in three parts: begin (workspace, metadata; false if there
@@ -133,10 +154,13 @@ private:
     // weights
     DevBuf conv0_w_, conv0_b_;
     std::vector<DevBuf> conv_w_, conv_b_, conv_gw_, conv_gb_;
-    DevBuf proj_lnw_, proj_lnb_, proj_w_, proj_b_;
+    DevBuf proj_lnw_, proj_lnb_, proj_b_;
+    LinearW proj_w_;
     DevBuf pos_w_, pos_b_, enc_lnw_, enc_lnb_;
     std::vector<LayerWeights> layers_;
-    DevBuf lm_w_, lm_b_;
+    LinearW lm_w_;
+    DevBuf lm_b_;
+    bool expand_weights_ = false;   // W2V_B200_EXPAND_WEIGHTS=1: every linear as fp16 rows
 
     // workspace
     DevBuf audio_stage_;                       // device copy of packed audio (run_host)

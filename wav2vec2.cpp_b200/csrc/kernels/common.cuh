@@ -81,6 +81,30 @@ W2V_DEV bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, uint64_t li
 W2V_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
     return mbar_wait_for(bar, parity, err, kWaitLimitNs);
 }
+// Bounded wait with cluster-scope acquire: for phases completed by arrivals
+// from the other CTA of a pair whose writes the waiter relies on.
+W2V_DEV bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+W2V_DEV bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    uint32_t spins = 0;
+    while (!mbar_try_wait_cluster(bar, parity)) {
+        if ((++spins & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+            report_error(err, kErrBarrierTimeout);
+            return false;
+        }
+    }
+    return true;
+}
 
 // ── TMA ────────────────────────────────────────────────────────────────────
 W2V_DEV void tma_prefetch_desc(const CUtensorMap* m) {

@@ -45,6 +45,49 @@ __global__ void dequant_q_kernel(const uint8_t* __restrict__ raw, int type, long
     }
 }
 
+// GGUF Q8_0 / Q4_0 blocks of rows [N, K] -> the fused GEMM's planes (layout
+// in qgemm_tc.cu): codes[n][k] int8 (Q8_0) or, per eight weights 8g..8g+7, a
+// 32-bit word holding weight 8g+2j in bits 4j..4j+3 and weight 8g+2j+1 in
+// bits 16+4j..19+4j, as the unsigned 4-bit code (Q4_0); scales[k/32][n] =
+// the block's fp16 scale bits.  One thread per block.
+__global__ void repack_q_kernel(const uint8_t* __restrict__ raw, int type, long long n_rows, long long K,
+                                uint8_t* __restrict__ codes, uint16_t* __restrict__ scales, long long ld_s) {
+    const long long nbr = K / 32;
+    const long long blk = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= n_rows * nbr) return;
+    const long long n = blk / nbr, j = blk - n * nbr;
+    if (type == 8) {
+        const uint8_t* b = raw + blk * 34;
+        scales[j * ld_s + n] = (uint16_t)(b[0] | (b[1] << 8));
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            w[i] = (uint32_t)b[2 + 4 * i] | ((uint32_t)b[3 + 4 * i] << 8) | ((uint32_t)b[4 + 4 * i] << 16) |
+                   ((uint32_t)b[5 + 4 * i] << 24);
+        uint4* dst = reinterpret_cast<uint4*>(codes + n * K + j * 32);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+        const uint8_t* b = raw + blk * 18;
+        scales[j * ld_s + n] = (uint16_t)(b[0] | (b[1] << 8));
+        uint32_t e[32];
+#pragma unroll
+        for (int t = 0; t < 16; t++) {
+            e[t] = b[2 + t] & 0xFu;
+            e[t + 16] = b[2 + t] >> 4;
+        }
+        uint32_t w[4];
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) v |= (e[8 * g + 2 * jj] << (4 * jj)) | (e[8 * g + 2 * jj + 1] << (16 + 4 * jj));
+            w[g] = v;
+        }
+        *reinterpret_cast<uint4*>(codes + n * (K / 2) + j * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
 __global__ void f32_to_f16_kernel(const float* __restrict__ in, long long n, __half* __restrict__ out) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) out[i] = __float2half_rn(in[i]);
@@ -772,6 +815,17 @@ extern "C" int w2v_dequant_f16(const void* raw, int type, long long n_rows, long
     const long long nb = n / 32;
     dequant_q_kernel<<<(unsigned)((nb + 127) / 128), 128, 0, S(stream)>>>((const uint8_t*)raw, type, nb,
                                                                           (__half*)out);
+    return launch_rc();
+}
+
+extern "C" int w2v_repack_q(const void* raw, int type, long long n_rows, long long K, void* codes, void* scales,
+                            long long ld_s, void* stream) {
+    if ((type != 2 && type != 8) || n_rows <= 0 || K <= 0 || K % 64 || ld_s < n_rows ||
+        (reinterpret_cast<uintptr_t>(codes) & 15) || (reinterpret_cast<uintptr_t>(scales) & 1))
+        return W2V_ERR_ARGS;
+    const long long nb = n_rows * (K / 32);
+    repack_q_kernel<<<(unsigned)((nb + 127) / 128), 128, 0, S(stream)>>>((const uint8_t*)raw, type, n_rows, K,
+                                                                         (uint8_t*)codes, (uint16_t*)scales, ld_s);
     return launch_rc();
 }
 
