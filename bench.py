@@ -658,6 +658,19 @@ def run_kernel_case(args):
         res = out.data_ptr() if epi == 3 else 0
         fn = lambda: K.gemm(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, out.data_ptr(), N, M, M,
                             bias.data_ptr(), res, N, epi, args.block_n, 0, st)
+        if args.weights != "f16":
+            # the same shape on quantised weights through the dequant-fused GEMM
+            import w2v_b200.synth as s
+            gt = 8 if args.weights == "q8_0" else 2
+            wq = (np.random.default_rng(0).standard_normal((N, Kd)) * 0.02).astype(np.float32)
+            raw = s.quantize_q8_0(wq) if gt == 8 else s.quantize_q4_0(wq)
+            raw_d = torch.from_numpy(np.frombuffer(raw, np.uint8).copy()).cuda()
+            ld = (N + 7) // 8 * 8
+            codes = torch.empty(N * Kd // (1 if gt == 8 else 2), dtype=torch.uint8, device="cuda")
+            scales = torch.zeros(Kd // 32, ld, dtype=torch.int16, device="cuda")
+            K.repack_q(raw_d.data_ptr(), gt, N, Kd, codes.data_ptr(), scales.data_ptr(), ld, st)
+            fn = lambda: K.gemm_q(A.data_ptr(), Kd, M, codes.data_ptr(), scales.data_ptr(), ld, gt, N, out.data_ptr(),
+                                  N, bias.data_ptr(), res, N, epi, args.block_n, 0, st)
         if epi == 4:
             # residual normalised on the fly from per-row (mean, rstd), in place over C
             stats = torch.stack([torch.randn(M), torch.rand(M) + 0.5], 1).cuda()
@@ -697,7 +710,7 @@ def run_kernel_case(args):
     ms = e0.elapsed_time(e1) / args.steps
     rec = {"kernel": args.kernel, "rows": M, "ms": ms, "tflops": flops / ms / 1e9}
     if args.kernel == "gemm":
-        rec.update(shape=args.gemm_shape, block_n=args.block_n)
+        rec.update(shape=args.gemm_shape, block_n=args.block_n, weights=args.weights)
     print(json.dumps(rec), flush=True)
 
 
@@ -723,6 +736,8 @@ def main():
     ap.add_argument("--gemm-shape", default="3072,768,1",
                     help="N,K,epilogue for --kernel gemm (epilogue 0 fp16, 1 fp16+GELU, 2 fp32, 3 fp32+residual, "
                          "4 fp32+LayerNorm-normalised residual)")
+    ap.add_argument("--weights", choices=["f16", "q8_0", "q4_0"], default="f16",
+                    help="B operand of --kernel gemm: fp16 rows, or quantised through the dequant-fused GEMM")
     ap.add_argument("--block-n", type=int, default=0,
                     help="GEMM tile for --kernel gemm: 0 automatic, 64/128/256 one CTA, -128/-256 CTA pair")
     args = ap.parse_args()

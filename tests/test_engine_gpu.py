@@ -61,7 +61,8 @@ def test_tiny_logits_vs_oracle(W, model_path, synth, arch, dtype):
 
 
 @pytest.mark.parametrize("case", ["base_q8_0_2s", "base_q4_0_2s", "base_f16_1s", "large_q8_0_1s",
-                                  "tiny_f16_1s", "tiny_pre_q4_0_1s", "base_q8_0_10s", "tiny80_f16_1s"])
+                                  "tiny_f16_1s", "tiny_pre_q4_0_1s", "base_q8_0_10s", "tiny80_f16_1s",
+                                  "large_q8_0_20s", "xlsr1b_f16_5s", "xlsr1b_f16_7s"])
 def test_logits_vs_reference_golden(W, model_path, synth, case):
     g = load_golden(case)
     m = model(W, golden_model(model_path, g))
@@ -75,6 +76,21 @@ def test_logits_vs_reference_golden(W, model_path, synth, case):
     # without bit-identical activations can come to the ggml path
     floor = np.abs(gg - ex).max()
     assert np.abs(got - gg).max() < max(2 * floor, TOL[g["dtype"]])
+
+
+def test_xlsr1b_ragged_batch_vs_reference_golden(W, model_path, synth):
+    """XLS-R-1B (48 pre-LN layers, hidden 1280, head dim 80, F16): its two
+    golden utterances (5 s and 7.3 s) in ONE ragged batch, each against the
+    reference's own single-utterance forward, and bit-identical to running
+    them one at a time."""
+    gs = [load_golden("xlsr1b_f16_5s"), load_golden("xlsr1b_f16_7s")]
+    m = model(W, golden_model(model_path, gs[0]))
+    xs = [synth.make_audio(int(g["seconds"] * 16000), int(g["seed"])) for g in gs]
+    batch = m.logits(xs)
+    for x, g, got in zip(xs, gs, batch):
+        assert got.shape == g["logits_exact"].shape
+        assert np.abs(got - g["logits_exact"]).max() < TOL["f16"]
+        assert np.array_equal(got, m.logits([x])[0])
 
 
 def test_stagewise_base_vs_oracle(W, model_path, synth):
@@ -219,3 +235,65 @@ def test_init_rejects_bad_model(W, tmp_path):
     bad.write_bytes(b"GGUF" + b"\0" * 10)
     with pytest.raises(W.EngineError):
         W.Model(bad)
+
+
+@pytest.mark.parametrize("arch,dtype,kw", [("tiny", "q8_0", {"bias_std": 0.02, "gain_jitter": 0.1}),
+                                           ("tiny_pre", "q4_0", {"bias_std": 0.02, "gain_jitter": 0.1}),
+                                           ("base", "q8_0", {}), ("base", "q4_0", {})])
+def test_quantised_linears_match_expanded_weights(W, model_path, synth, arch, dtype, kw, monkeypatch):
+    """Q8_0 / Q4_0 linears stay quantised on the device (code + scale planes,
+    expanded inside the fused GEMM).  Their logits agree with those of the
+    same model with every linear expanded to fp16 rows at load
+    (W2V_B200_EXPAND_WEIGHTS=1) -- same fp16 weights, so only the tensor
+    core's summation order differs -- and the device holds a fraction of the
+    bytes."""
+    p = model_path(arch, dtype, **kw)
+    mq = W.Model(p)
+    monkeypatch.setenv("W2V_B200_EXPAND_WEIGHTS", "1")
+    mf = W.Model(p)
+    monkeypatch.delenv("W2V_B200_EXPAND_WEIGHTS")
+    lens = [160000, 51234, 16000] if arch == "base" else [16000, 7000, 400]
+    xs = [synth.make_audio(n, 400 + i) for i, n in enumerate(lens)]
+    a, b = mq.logits(xs), mf.logits(xs)
+    worst = 0.0
+    for u, v in zip(a, b):
+        assert u.shape == v.shape
+        worst = max(worst, float(np.abs(u - v).max()))
+    print(f"{arch} {dtype}: max |quantised - expanded| = {worst:.2e}")
+    assert worst < 5e-3
+    # ragged batch == one utterance at a time, bit for bit, on the quantised path too
+    assert np.array_equal(a[1], mq.logits([xs[1]])[0])
+    nq, nf = mq.linear_weight_bytes(), mf.linear_weight_bytes()
+    assert nq < nf
+    if arch == "base":
+        # linear weights: fp16 rows 170.7 MB; codes (1 or 1/2 byte) + one fp16 scale per 32
+        params = 12 * (4 * 768 * 768 + 2 * 768 * 3072) + 768 * 512 + 32 * 768     # 85_352_448
+        assert nf == 2 * params
+        assert nq == params * (1 if dtype == "q8_0" else 0.5) + params // 32 * 2
+    mq.close()
+    mf.close()
+
+
+def test_word_timestamps_match_reference_post_processing(W, model_path, synth):
+    """Words and their times from the GPU spans (wav2vec2_transcribe_batch with
+    word timestamps) equal the reference's own ids_to_text / spans_to_words
+    (src/wav2vec2.cpp:400-452, built from its source in oracle/_ref) run on
+    the same logits."""
+    if not O.ref_available():
+        pytest.skip("reference oracle build absent")
+    for arch, dtype, kw, lens in (("tiny_pre", "q4_0", {"bias_std": 0.02, "gain_jitter": 0.1}, [16000, 30000, 5000]),
+                                  ("base", "q8_0", {}, [160000])):
+        p = model_path(arch, dtype, **kw)
+        m = model(W, p)
+        ref = O.RefOracle(p)
+        xs = [synth.make_audio(n, 640 + i) for i, n in enumerate(lens)]
+        res = m.transcribe_batch(xs, word_timestamps=True)
+        n_words = 0
+        for x, r in zip(xs, res):
+            text, words = O.ref_words_from_logits(ref, m.logits([x])[0])
+            assert r["text"] == text
+            assert r["words"] == words
+            n_words += len(words)
+        assert n_words > 0
+        single = m.transcribe(xs[0], word_timestamps=True)
+        assert single["words"] == res[0]["words"]
