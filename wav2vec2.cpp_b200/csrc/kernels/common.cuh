@@ -402,6 +402,14 @@ W2V_DEV uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
 W2V_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Arrive on an mbarrier of either CTA of the pair with the default (CTA-scope)
+// release.  For hand-offs whose payload is tensor-memory state ordered by
+// tcgen05.fence::before_thread_sync: a cluster-scope release would also make
+// the arriving thread wait until all of its earlier global stores are
+// performed, which stalls an epilogue that has just issued thousands.
+W2V_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 W2V_DEV void mbar_arrive_expect_tx_addr(uint32_t saddr, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr), "r"(bytes) : "memory");
 }

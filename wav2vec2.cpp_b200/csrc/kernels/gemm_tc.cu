@@ -696,7 +696,7 @@ gemm2_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(tempty_lead + (uint32_t)(ab * 8));
+            if (lane == 0) mbar_arrive_remote(tempty_lead + (uint32_t)(ab * 8));
         }
         if (kF16 && p.tma_c) {   // the stores are complete before the CTA exits
             if (lane == 0) bulk_wait_group<0>();

@@ -323,7 +323,7 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    if constexpr (PAIR) mbar_arrive_cluster(afull_lead + (uint32_t)(f * 8));
+                    if constexpr (PAIR) mbar_arrive_remote(afull_lead + (uint32_t)(f * 8));
                     else mbar_arrive(&afull[f]);
                 }
             }
@@ -354,41 +354,48 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
-                        if constexpr (PAIR) mbar_arrive_cluster(tempty_lead + (uint32_t)(ab * 8));
+                        if constexpr (PAIR) mbar_arrive_remote(tempty_lead + (uint32_t)(ab * 8));
                         else mbar_arrive(&tempty[ab]);
                     }
                 }
                 const int r0 = ri * BN + c * 32;
                 if (r0 >= p.m_valid) continue;
-                float2 st = make_float2(0.f, 0.f);
-                if (EPI == W2V_EPI_F32_RESID_LN && r0 + lane < p.m_valid) st = p.ln_stats[r0 + lane];
+                if (EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU) {
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    const int r = r0 + j;
-                    float a = v[j] + bias, b = v[j + 1] + bias;
-                    const bool v0 = fv && r < p.m_valid, v1 = fv && r + 1 < p.m_valid;
-                    if (EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU) {
+                    for (int j = 0; j < 32; j += 2) {
+                        const int r = r0 + j;
+                        const float a = v[j] + bias, b = v[j + 1] + bias;
                         const uint32_t h = EPI == W2V_EPI_F16_GELU ? gelu_half2(a, b) : pack_half2(a, b);
                         __half* cp = reinterpret_cast<__half*>(p.C) + (long long)r * p.ldc + fcol;
-                        if (v0) *reinterpret_cast<uint16_t*>(cp) = (uint16_t)(h & 0xFFFFu);
-                        if (v1) *reinterpret_cast<uint16_t*>(cp + p.ldc) = (uint16_t)(h >> 16);
-                    } else {
-                        float* cp = reinterpret_cast<float*>(p.C) + (long long)r * p.ldc + fcol;
-                        const float* rp = p.resid + (long long)r * p.ldr + fcol;
-                        if (EPI == W2V_EPI_F32_RESID) {
-                            if (v0) a += rp[0];
-                            if (v1) b += rp[p.ldr];
-                        }
-                        if (EPI == W2V_EPI_F32_RESID_LN) {
-                            const float m0 = __shfl_sync(0xffffffffu, st.x, j), s0 = __shfl_sync(0xffffffffu, st.y, j);
-                            const float m1 = __shfl_sync(0xffffffffu, st.x, j + 1);
-                            const float s1 = __shfl_sync(0xffffffffu, st.y, j + 1);
-                            if (v0) a += (rp[0] - m0) * s0 * lw + lb;
-                            if (v1) b += (rp[p.ldr] - m1) * s1 * lw + lb;
-                        }
-                        if (v0) cp[0] = a;
-                        if (v1) cp[p.ldc] = b;
+                        if (fv && r < p.m_valid) *reinterpret_cast<uint16_t*>(cp) = (uint16_t)(h & 0xFFFFu);
+                        if (fv && r + 1 < p.m_valid) *reinterpret_cast<uint16_t*>(cp + p.ldc) = (uint16_t)(h >> 16);
                     }
+                } else {
+                    // C may alias the residual (in place): every residual value of the
+                    // chunk is loaded before the first store, so the loads are issued
+                    // back to back instead of one L2 round trip per row.
+                    float rv[32];
+                    if (EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) {
+                        const float* rp = p.resid + (long long)r0 * p.ldr + fcol;
+#pragma unroll
+                        for (int j = 0; j < 32; j++) rv[j] = (fv && r0 + j < p.m_valid) ? rp[(long long)j * p.ldr] : 0.f;
+                    }
+                    float2 st = make_float2(0.f, 0.f);
+                    if (EPI == W2V_EPI_F32_RESID_LN && r0 + lane < p.m_valid) st = p.ln_stats[r0 + lane];
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        float a = v[j] + bias;
+                        if (EPI == W2V_EPI_F32_RESID) a += rv[j];
+                        if (EPI == W2V_EPI_F32_RESID_LN) {
+                            const float m = __shfl_sync(0xffffffffu, st.x, j), sd = __shfl_sync(0xffffffffu, st.y, j);
+                            a += (rv[j] - m) * sd * lw + lb;
+                        }
+                        v[j] = a;
+                    }
+                    float* cp = reinterpret_cast<float*>(p.C) + (long long)r0 * p.ldc + fcol;
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (fv && r0 + j < p.m_valid) cp[(long long)j * p.ldc] = v[j];
                 }
             }
         }
