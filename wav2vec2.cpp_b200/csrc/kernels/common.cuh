@@ -288,9 +288,10 @@ W2V_DEV uint32_t pack_half2(float a, float b) {
 
 // gelu_tanh of two values, rounded to a packed fp16 pair: the tanh form
 // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) evaluated entirely on fp16
-// pairs once x is rounded to fp16 (as the reference model does: it evaluates
-// GELU from a table indexed by the fp16 input), six pair instructions and one
-// of them on the special-function unit.  Error within 2e-3 (1 + |gelu(x)|),
+// pairs once x is rounded to fp16, six pair instructions and one of them on
+// the special-function unit.  The reference evaluates the same formula with
+// fp32 tanhf (src/ops.h:18-21); this is a deliberate precision trade for
+// outputs that are stored as fp16 anyway: error within 2e-3 (1 + |gelu(x)|),
 // about twice the fp16 rounding of the result.  Large |x|: x^2 and the tanh
 // argument saturate to +-inf (tanh -> +-1), giving x or 0.
 W2V_DEV uint32_t gelu_f16x2(uint32_t x) {

@@ -52,6 +52,7 @@ struct QParams {
     int m_valid;         // activation rows
     int N;               // weight rows = output features
     int f_tiles, r_tiles, k_blocks;
+    int pack2;           // fp16 C: pairs of features may be stored as one 4-byte word
     void* C;
     long long ldc;
     const float* bias;
@@ -332,6 +333,8 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
         // epilogue: lane = output feature, the 32 registers of a chunk = 32 activation rows
         const int q = warp & 3;
         const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0u;
+        constexpr bool kRes = EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN;
+        constexpr int kNch = BN / 32;
         int it = 0;
         for (int tile = unit; tile < total; tile += n_units, it++) {
             const int fi = tile % p.f_tiles, ri = tile / p.f_tiles;
@@ -342,14 +345,30 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
             const float bias = (p.bias && fv) ? __ldg(p.bias + fcol) : 0.f;
             float lw = 0.f, lb = 0.f;
             if (EPI == W2V_EPI_F32_RESID_LN && fv) { lw = __ldg(p.ln_w + fcol); lb = __ldg(p.ln_b + fcol); }
+            // The residual does not depend on the MMA: chunk c+1's residual (and its
+            // rows' LayerNorm statistics) is in flight while chunk c is computed, and
+            // chunk 0's while the accumulator is awaited.  Chunks cover distinct rows,
+            // so reading ahead never crosses the in-place stores.
+            float rn[32];
+            float2 stn = make_float2(0.f, 0.f);
+            auto fetch = [&](int c) {
+                const int r0 = ri * BN + c * 32;
+                if constexpr (kRes) {
+                    const float* rp = p.resid + (long long)r0 * p.ldr + fcol;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) rn[j] = (fv && r0 + j < p.m_valid) ? rp[(long long)j * p.ldr] : 0.f;
+                }
+                if (EPI == W2V_EPI_F32_RESID_LN) stn = r0 + lane < p.m_valid ? p.ln_stats[r0 + lane] : make_float2(0.f, 0.f);
+            };
+            if (kRes) fetch(0);
             if (!mbar_wait(&tfull[ab], aph, p.err)) break;
             tc_fence_after();
             const uint32_t tacc = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; c++) {
+            for (int c = 0; c < kNch; c++) {
                 float v[32];
                 tmem_ld32(tacc + (uint32_t)(c * 32), v);
-                if (c == BN / 32 - 1) {
+                if (c == kNch - 1) {
                     // the accumulator is in registers: hand it back to the MMA
                     tc_fence_before();
                     __syncwarp();
@@ -359,29 +378,39 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                     }
                 }
                 const int r0 = ri * BN + c * 32;
+                float rv[32];
+                float2 st = stn;
+                if constexpr (kRes) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) rv[j] = rn[j];
+                    if (c + 1 < kNch && r0 + 32 < p.m_valid) fetch(c + 1);
+                }
                 if (r0 >= p.m_valid) continue;
                 if (EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU) {
+                    // rows j, j+1 of this lane's feature as one fp16 pair; one shuffle
+                    // with the neighbouring lane turns them into features (f, f+1) of
+                    // row j (even lanes) or row j+1 (odd lanes): 4-byte stores
+                    const bool odd = lane & 1;
+                    const int fpair = fcol - (odd ? 1 : 0);
+                    const bool pv = fpair + 1 < p.N;      // both features of the pair exist
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
-                        const int r = r0 + j;
                         const float a = v[j] + bias, b = v[j + 1] + bias;
                         const uint32_t h = EPI == W2V_EPI_F16_GELU ? gelu_half2(a, b) : pack_half2(a, b);
-                        __half* cp = reinterpret_cast<__half*>(p.C) + (long long)r * p.ldc + fcol;
-                        if (fv && r < p.m_valid) *reinterpret_cast<uint16_t*>(cp) = (uint16_t)(h & 0xFFFFu);
-                        if (fv && r + 1 < p.m_valid) *reinterpret_cast<uint16_t*>(cp + p.ldc) = (uint16_t)(h >> 16);
+                        const uint32_t o = __shfl_xor_sync(0xffffffffu, h, 1);
+                        const uint32_t w = odd ? __byte_perm(o, h, 0x7632) : __byte_perm(h, o, 0x5410);
+                        const int r = r0 + j + (odd ? 1 : 0);
+                        __half* cp = reinterpret_cast<__half*>(p.C) + (long long)r * p.ldc + fpair;
+                        if (r < p.m_valid) {
+                            if (pv && p.pack2) {
+                                *reinterpret_cast<uint32_t*>(cp) = w;
+                            } else {
+                                if (fpair < p.N) *reinterpret_cast<uint16_t*>(cp) = (uint16_t)(w & 0xFFFFu);
+                                if (fpair + 1 < p.N) *reinterpret_cast<uint16_t*>(cp + 1) = (uint16_t)(w >> 16);
+                            }
+                        }
                     }
                 } else {
-                    // C may alias the residual (in place): every residual value of the
-                    // chunk is loaded before the first store, so the loads are issued
-                    // back to back instead of one L2 round trip per row.
-                    float rv[32];
-                    if (EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) {
-                        const float* rp = p.resid + (long long)r0 * p.ldr + fcol;
-#pragma unroll
-                        for (int j = 0; j < 32; j++) rv[j] = (fv && r0 + j < p.m_valid) ? rp[(long long)j * p.ldr] : 0.f;
-                    }
-                    float2 st = make_float2(0.f, 0.f);
-                    if (EPI == W2V_EPI_F32_RESID_LN && r0 + lane < p.m_valid) st = p.ln_stats[r0 + lane];
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         float a = v[j] + bias;
@@ -567,6 +596,7 @@ static int qgemm_impl(const void* A, long long K, long long M, const void* Bq, c
     p.k_blocks = (int)(K / kBK);
     p.C = C;
     p.ldc = ldc;
+    p.pack2 = !(ldc & 1) && !(reinterpret_cast<uintptr_t>(C) & 3);
     p.bias = bias;
     p.resid = resid;
     p.ldr = ldr;
