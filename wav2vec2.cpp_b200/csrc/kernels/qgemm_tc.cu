@@ -52,7 +52,6 @@ struct QParams {
     int m_valid;         // activation rows
     int N;               // weight rows = output features
     int f_tiles, r_tiles, k_blocks;
-    int pack2;           // fp16 C: pairs of features may be stored as one 4-byte word
     void* C;
     long long ldc;
     const float* bias;
@@ -387,28 +386,14 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                 }
                 if (r0 >= p.m_valid) continue;
                 if (EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU) {
-                    // rows j, j+1 of this lane's feature as one fp16 pair; one shuffle
-                    // with the neighbouring lane turns them into features (f, f+1) of
-                    // row j (even lanes) or row j+1 (odd lanes): 4-byte stores
-                    const bool odd = lane & 1;
-                    const int fpair = fcol - (odd ? 1 : 0);
-                    const bool pv = fpair + 1 < p.N;      // both features of the pair exist
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
+                        const int r = r0 + j;
                         const float a = v[j] + bias, b = v[j + 1] + bias;
                         const uint32_t h = EPI == W2V_EPI_F16_GELU ? gelu_half2(a, b) : pack_half2(a, b);
-                        const uint32_t o = __shfl_xor_sync(0xffffffffu, h, 1);
-                        const uint32_t w = odd ? __byte_perm(o, h, 0x7632) : __byte_perm(h, o, 0x5410);
-                        const int r = r0 + j + (odd ? 1 : 0);
-                        __half* cp = reinterpret_cast<__half*>(p.C) + (long long)r * p.ldc + fpair;
-                        if (r < p.m_valid) {
-                            if (pv && p.pack2) {
-                                *reinterpret_cast<uint32_t*>(cp) = w;
-                            } else {
-                                if (fpair < p.N) *reinterpret_cast<uint16_t*>(cp) = (uint16_t)(w & 0xFFFFu);
-                                if (fpair + 1 < p.N) *reinterpret_cast<uint16_t*>(cp + 1) = (uint16_t)(w >> 16);
-                            }
-                        }
+                        __half* cp = reinterpret_cast<__half*>(p.C) + (long long)r * p.ldc + fcol;
+                        if (fv && r < p.m_valid) *reinterpret_cast<uint16_t*>(cp) = (uint16_t)(h & 0xFFFFu);
+                        if (fv && r + 1 < p.m_valid) *reinterpret_cast<uint16_t*>(cp + p.ldc) = (uint16_t)(h >> 16);
                     }
                 } else {
 #pragma unroll
@@ -596,7 +581,6 @@ static int qgemm_impl(const void* A, long long K, long long M, const void* Bq, c
     p.k_blocks = (int)(K / kBK);
     p.C = C;
     p.ldc = ldc;
-    p.pack2 = !(ldc & 1) && !(reinterpret_cast<uintptr_t>(C) & 3);
     p.bias = bias;
     p.resid = resid;
     p.ldr = ldr;
