@@ -52,6 +52,7 @@ struct QParams {
     int m_valid;         // activation rows
     int N;               // weight rows = output features
     int f_tiles, r_tiles, k_blocks;
+    int tma;             // epilogue through shared-memory boxes and TMA (tmC, tmR); else direct stores
     void* C;
     long long ldc;
     const float* bias;
@@ -70,10 +71,12 @@ struct QCfg {
     static constexpr int kCodeBytes = kRows * code_row_bytes(WQ);
     static constexpr int kScaleBytes = 2 * kRows * 2;
     static constexpr int kPer = kXBytes + kCodeBytes + kScaleBytes;
-    static constexpr int kStages = cmin(8, (kSmemCap - 1024 - 512) / kPer);
+    static constexpr int kEpiBytes = kNE * 16384;   // per epilogue warp: two output and two residual boxes
+    static constexpr int kStages = cmin(8, (kSmemCap - 1024 - 512 - kEpiBytes) / kPer);
     static constexpr int kOffCode = kStages * kXBytes;
     static constexpr int kOffScale = kOffCode + kStages * kCodeBytes;
-    static constexpr int kOffBar = kOffScale + kStages * kScaleBytes;
+    static constexpr int kOffEpi = kOffScale + kStages * kScaleBytes;
+    static constexpr int kOffBar = kOffEpi + kEpiBytes;
     static constexpr int kSmem = kOffBar + 512 + 1024;
     static constexpr int kSB = cmin(4, (512 - 2 * BN) / 32);   // weight tiles in TMEM
     static constexpr int kACol = 2 * BN;                        // first weight-tile column
@@ -102,6 +105,13 @@ W2V_DEV void umma_f16_pair_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_d
         : "memory");
 }
 
+W2V_DEV void tma_store_2d(const CUtensorMap* m, const void* smem_src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
 W2V_DEV uint32_t hsub2_u32(uint32_t a, uint32_t b) {
     uint32_t d;
     asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
@@ -128,7 +138,8 @@ W2V_DEV void q4_word(uint32_t w, uint32_t dd, uint32_t* o) {
 template <int BN, int EPI, int WQ, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmQ,
-             const __grid_constant__ CUtensorMap tmS, QParams p) {
+             const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmC,
+             const __grid_constant__ CUtensorMap tmR, QParams p) {
     using Cfg = QCfg<BN, WQ, PAIR>;
     constexpr int S = Cfg::kStages, SB = Cfg::kSB, CT = PAIR ? 2 : 1;
     extern __shared__ uint8_t smem_raw[];
@@ -146,7 +157,8 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
     uint64_t* tfull = aempty + SB;         // accumulator b ready (each CTA)
     uint64_t* tempty = tfull + 2;          // accumulator b drained (pair: leader, both CTAs' epilogues)
     uint64_t* done = tempty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* rbar = done + 1;             // residual box b of epilogue warp w landed: rbar[2 w + b]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * kNE);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
@@ -159,6 +171,7 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
         for (int f = 0; f < SB; f++) { mbar_init(&afull[f], kNC * CT); mbar_init(&aempty[f], 1); }
         for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], kNE * CT); }
         mbar_init(done, 1);
+        for (int i = 0; i < 2 * kNE; i++) mbar_init(&rbar[i], 1);
         fence_mbar_init();
         tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmQ);
@@ -331,6 +344,131 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
     } else {
         // epilogue: lane = output feature, the 32 registers of a chunk = 32 activation rows
         const int q = warp & 3;
+        if (p.tma) {
+            // Staged: per 32 x 32 chunk, the residual box arrives by TMA one chunk
+            // ahead (two boxes per warp), and the results go through one of two
+            // output boxes and a TMA tile store.  Register j of lane f is row j,
+            // feature f of the box: each shared-memory access of the warp touches
+            // one contiguous 64- or 128-byte box row, so none conflicts on a bank.
+            constexpr bool kRes = EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN;
+            constexpr bool kF16 = EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU;
+            constexpr int kNch = BN / 32;
+            uint8_t* ebase = smem + Cfg::kOffEpi + (warp - 2) * 16384;
+            float* rbox = reinterpret_cast<float*>(ebase + 8192);
+            uint64_t* rb = rbar + 2 * (warp - 2);
+            const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0u;
+            uint32_t nst = 0, nrl = 0, nrw = 0;   // output boxes stored, residual boxes requested / awaited
+            int it = 0;
+            for (int tile = unit; tile < total; tile += n_units, it++) {
+                const int fi = tile % p.f_tiles, ri = tile / p.f_tiles;
+                const int ab = it & 1;
+                const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+                const int fcol0 = fi * kRows * CT + (int)rank * kRows + 32 * q;
+                const int fcol = fcol0 + lane;
+                const bool fv = fcol < p.N;
+                const float bias = (p.bias && fv) ? __ldg(p.bias + fcol) : 0.f;
+                float lw = 0.f, lb = 0.f;
+                if (EPI == W2V_EPI_F32_RESID_LN && fv) { lw = __ldg(p.ln_w + fcol); lb = __ldg(p.ln_b + fcol); }
+                if (fcol0 >= p.N) {
+                    // every feature of this warp's quarter is past the last one: nothing to
+                    // load or store, only the accumulator to hand back
+                    if (!mbar_wait(&tfull[ab], aph, p.err)) break;
+                    tc_fence_after();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if constexpr (PAIR) mbar_arrive_remote(tempty_lead + (uint32_t)(ab * 8));
+                        else mbar_arrive(&tempty[ab]);
+                    }
+                    continue;
+                }
+                auto request = [&](int c) {          // residual box of chunk c (lane 0)
+                    const uint32_t b = nrl & 1u;
+                    fence_async_smem();              // earlier reads of this box precede the TMA write
+                    mbar_arrive_expect_tx(&rb[b], 32 * 32 * 4);
+                    tma_load_2d(rbox + b * 1024, &tmR, &rb[b], fcol0, ri * BN + c * 32);
+                };
+                const uint32_t rfirst = nrl;
+                if constexpr (kRes) {
+                    if (lane == 0) request(0);
+                    nrl++;
+                }
+                float2 stn = make_float2(0.f, 0.f);
+                if (EPI == W2V_EPI_F32_RESID_LN && ri * BN + lane < p.m_valid) stn = p.ln_stats[ri * BN + lane];
+                if (!mbar_wait(&tfull[ab], aph, p.err)) break;
+                tc_fence_after();
+                const uint32_t tacc = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * BN);
+                bool ok = true;
+#pragma unroll 1
+                for (int c = 0; c < kNch; c++) {
+                    float v[32];
+                    tmem_ld32(tacc + (uint32_t)(c * 32), v);
+                    if (c == kNch - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            if constexpr (PAIR) mbar_arrive_remote(tempty_lead + (uint32_t)(ab * 8));
+                            else mbar_arrive(&tempty[ab]);
+                        }
+                    }
+                    const int r0 = ri * BN + c * 32;
+                    if (r0 >= p.m_valid) continue;
+                    const float2 st = stn;
+                    if (EPI == W2V_EPI_F32_RESID_LN && c + 1 < kNch)
+                        stn = r0 + 32 + lane < p.m_valid ? p.ln_stats[r0 + 32 + lane] : make_float2(0.f, 0.f);
+                    const float* rcur = rbox;
+                    if constexpr (kRes) {
+                        const uint32_t idx = rfirst + (uint32_t)c;
+                        if (c + 1 < kNch && r0 + 32 < p.m_valid) {
+                            __syncwarp();            // every lane is done with the box chunk c+1 reuses
+                            if (lane == 0) request(c + 1);
+                            nrl++;
+                        }
+                        if (!mbar_wait(&rb[idx & 1u], (idx >> 1) & 1u, p.err)) { ok = false; break; }
+                        nrw = idx + 1;
+                        rcur = rbox + (idx & 1u) * 1024;
+                    }
+                    uint8_t* ob = ebase + (nst & 1u) * 4096;
+                    if (lane == 0) bulk_wait_group_read<1>();   // the store issued from this box two boxes ago has read it
+                    __syncwarp();
+                    if constexpr (kF16) {
+                        __half* oh = reinterpret_cast<__half*>(ob);
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            const float a = v[j] + bias, b = v[j + 1] + bias;
+                            const uint32_t h = EPI == W2V_EPI_F16_GELU ? gelu_half2(a, b) : pack_half2(a, b);
+                            reinterpret_cast<uint16_t*>(oh)[j * 32 + lane] = (uint16_t)(h & 0xFFFFu);
+                            reinterpret_cast<uint16_t*>(oh)[(j + 1) * 32 + lane] = (uint16_t)(h >> 16);
+                        }
+                    } else {
+                        float* of = reinterpret_cast<float*>(ob);
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            float a = v[j] + bias;
+                            if (EPI == W2V_EPI_F32_RESID) a += rcur[j * 32 + lane];
+                            if (EPI == W2V_EPI_F32_RESID_LN) {
+                                const float m = __shfl_sync(0xffffffffu, st.x, j), sd = __shfl_sync(0xffffffffu, st.y, j);
+                                a += (rcur[j * 32 + lane] - m) * sd * lw + lb;
+                            }
+                            of[j * 32 + lane] = a;
+                        }
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmC, ob, fcol0, r0);
+                        bulk_commit_group();
+                    }
+                    nst++;
+                }
+                if (!ok) break;
+            }
+            // the stores have completed and no residual box is still being written
+            // (after an expired wait boxes may have been requested and not awaited)
+            for (uint32_t idx = nrw; idx < nrl; idx++) mbar_wait(&rb[idx & 1u], (idx >> 1) & 1u, p.err);
+            if (lane == 0) bulk_wait_group<0>();
+            __syncwarp();
+        } else {
         const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0u;
         constexpr bool kRes = EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN;
         constexpr int kNch = BN / 32;
@@ -415,6 +553,8 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
         }
     }
 
+    }
+
     tc_fence_before();
     if (PAIR) cluster_sync_all(); else __syncthreads();
     if (warp == 1) {
@@ -445,8 +585,8 @@ static int sm_count() {
 }
 
 template <int BN, int EPI, int WQ, bool PAIR>
-static int launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts, const QParams& p,
-                  cudaStream_t st) {
+static int launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts, const CUtensorMap& tc,
+                  const CUtensorMap& tr, const QParams& p, cudaStream_t st) {
     using Cfg = QCfg<BN, WQ, PAIR>;
     auto kern = qgemm_kernel<BN, EPI, WQ, PAIR>;
     static int max_units[64] = {};
@@ -479,26 +619,27 @@ static int launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMa
     const int total = p.f_tiles * p.r_tiles;
     const int units = total < max_units[dev & 63] ? total : max_units[dev & 63];
     cfg.gridDim = dim3((unsigned)(units * (PAIR ? 2 : 1)), 1, 1);
-    if (cudaLaunchKernelEx(&cfg, kern, tx, tq, ts, p) != cudaSuccess) return W2V_ERR_LAUNCH;
+    if (cudaLaunchKernelEx(&cfg, kern, tx, tq, ts, tc, tr, p) != cudaSuccess) return W2V_ERR_LAUNCH;
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
 template <int EPI, int WQ>
 static int launch_tile(int bn, const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts,
-                       const QParams& p, cudaStream_t st) {
+                       const CUtensorMap& tc, const CUtensorMap& tr, const QParams& p, cudaStream_t st) {
     switch (bn) {
-        case -192: return launch<192, EPI, WQ, true>(tx, tq, ts, p, st);
-        case -128: return launch<128, EPI, WQ, true>(tx, tq, ts, p, st);
-        case 192: return launch<192, EPI, WQ, false>(tx, tq, ts, p, st);
-        case 128: return launch<128, EPI, WQ, false>(tx, tq, ts, p, st);
+        case -192: return launch<192, EPI, WQ, true>(tx, tq, ts, tc, tr, p, st);
+        case -128: return launch<128, EPI, WQ, true>(tx, tq, ts, tc, tr, p, st);
+        case 192: return launch<192, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
+        case 128: return launch<128, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
         default: return W2V_ERR_ARGS;
     }
 }
 
 template <int EPI>
 static int launch_w(int wq, int bn, const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts,
-                    const QParams& p, cudaStream_t st) {
-    return wq == kQ8 ? launch_tile<EPI, kQ8>(bn, tx, tq, ts, p, st) : launch_tile<EPI, kQ4>(bn, tx, tq, ts, p, st);
+                    const CUtensorMap& tc, const CUtensorMap& tr, const QParams& p, cudaStream_t st) {
+    return wq == kQ8 ? launch_tile<EPI, kQ8>(bn, tx, tq, ts, tc, tr, p, st)
+                     : launch_tile<EPI, kQ4>(bn, tx, tq, ts, tc, tr, p, st);
 }
 
 // Tile: CTA pairs (256 weight rows per tile) or single CTAs (128), each over
@@ -573,7 +714,32 @@ static int qgemm_impl(const void* A, long long K, long long M, const void* Bq, c
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return W2V_ERR_TENSOR_MAP;
     }
+    // C and the residual as 32 x 32 boxes for the staged epilogue: fp16 C needs N
+    // and ldc multiples of 8, fp32 C and the residual multiples of 4 (a store
+    // clips the innermost dimension at 16-byte granularity only)
+    const bool f16 = epilogue == W2V_EPI_F16 || epilogue == W2V_EPI_F16_GELU;
+    const bool res = epilogue == W2V_EPI_F32_RESID || epilogue == W2V_EPI_F32_RESID_LN;
+    bool tma = (reinterpret_cast<uintptr_t>(C) & 15) == 0 && (f16 ? (N % 8 == 0 && ldc % 8 == 0) : (N % 4 == 0 && ldc % 4 == 0));
+    if (res) tma = tma && (reinterpret_cast<uintptr_t>(resid) & 15) == 0 && ldr % 4 == 0;
+    CUtensorMap tc = tx, tr = tx;
+    if (tma) {
+        const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+        const uint64_t str[1] = {(uint64_t)ldc * (f16 ? 2 : 4)};
+        const uint32_t box[2] = {32, 32};
+        if (enc(&tc, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, C, dims, str, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return W2V_ERR_TENSOR_MAP;
+        if (res) {
+            const uint64_t rstr[1] = {(uint64_t)ldr * 4};
+            if (enc(&tr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(resid), dims, rstr, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return W2V_ERR_TENSOR_MAP;
+        }
+    }
     QParams p;
+    p.tma = tma ? 1 : 0;
     p.m_valid = (int)M;
     p.N = N;
     p.f_tiles = (N + kRows * (pair ? 2 : 1) - 1) / (kRows * (pair ? 2 : 1));
@@ -590,11 +756,11 @@ static int qgemm_impl(const void* A, long long K, long long M, const void* Bq, c
     p.err = err;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     switch (epilogue) {
-        case W2V_EPI_F16: return launch_w<W2V_EPI_F16>(wq, bn, tx, tq, ts, p, st);
-        case W2V_EPI_F16_GELU: return launch_w<W2V_EPI_F16_GELU>(wq, bn, tx, tq, ts, p, st);
-        case W2V_EPI_F32: return launch_w<W2V_EPI_F32>(wq, bn, tx, tq, ts, p, st);
-        case W2V_EPI_F32_RESID: return launch_w<W2V_EPI_F32_RESID>(wq, bn, tx, tq, ts, p, st);
-        default: return launch_w<W2V_EPI_F32_RESID_LN>(wq, bn, tx, tq, ts, p, st);
+        case W2V_EPI_F16: return launch_w<W2V_EPI_F16>(wq, bn, tx, tq, ts, tc, tr, p, st);
+        case W2V_EPI_F16_GELU: return launch_w<W2V_EPI_F16_GELU>(wq, bn, tx, tq, ts, tc, tr, p, st);
+        case W2V_EPI_F32: return launch_w<W2V_EPI_F32>(wq, bn, tx, tq, ts, tc, tr, p, st);
+        case W2V_EPI_F32_RESID: return launch_w<W2V_EPI_F32_RESID>(wq, bn, tx, tq, ts, tc, tr, p, st);
+        default: return launch_w<W2V_EPI_F32_RESID_LN>(wq, bn, tx, tq, ts, tc, tr, p, st);
     }
 }
 
