@@ -107,7 +107,7 @@ def run_pair(K, q, M, epi, bn, seed):
     (499, 3072, 768, EPI_F16_GELU, 0), (499, 32, 768, EPI_F32, 0), (1, 128, 64, EPI_F32, 128),
     (31936, 2304, 768, EPI_F16, -192), (5000, 768, 3072, EPI_F32_RESID, -192), (777, 1024, 1024, EPI_F32, 128),
     (300, 768, 768, EPI_F32_RESID, -128), (2049, 200, 512, EPI_F16, 192), (130, 96, 256, EPI_F16_GELU, -128),
-    (4000, 3072, 768, EPI_F16_GELU, 0)])
+    (4000, 3072, 768, EPI_F16_GELU, 0), (3001, 768, 768, EPI_F32_RESID, -224), (700, 320, 512, EPI_F16, 224)])
 def test_gemm_q_matches_fp16_gemm(K, synth, gtype, M, N, Kd, epi, bn):
     """Every tile family (CTA pairs and single CTAs, 192 and 128 activation
     rows), ragged rows and features, every epilogue."""

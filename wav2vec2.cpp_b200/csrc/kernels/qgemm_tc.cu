@@ -627,6 +627,8 @@ template <int EPI, int WQ>
 static int launch_tile(int bn, const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts,
                        const CUtensorMap& tc, const CUtensorMap& tr, const QParams& p, cudaStream_t st) {
     switch (bn) {
+        case -224: return launch<224, EPI, WQ, true>(tx, tq, ts, tc, tr, p, st);
+        case 224: return launch<224, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
         case -192: return launch<192, EPI, WQ, true>(tx, tq, ts, tc, tr, p, st);
         case -128: return launch<128, EPI, WQ, true>(tx, tq, ts, tc, tr, p, st);
         case 192: return launch<192, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
@@ -644,8 +646,20 @@ static int launch_w(int wq, int bn, const CUtensorMap& tx, const CUtensorMap& tq
 
 // Tile: CTA pairs (256 weight rows per tile) or single CTAs (128), each over
 // 192 or 128 activation rows.  Each SM computes 128 weight rows x BN rows per
-// tile either way; pick the fewest waves of tiles over the SMs, weighted by
-// the tile's width, preferring pairs (half the activation bytes per SM).
+// tile either way.  Estimated time = waves of tiles over the SMs x tile width
+// x the measured time per activation row of that tile (B200, the base
+// encoder linears at 31936 rows: 192-row tiles stage fewer operand bytes per
+// MAC than 128-row ones, 1.36x faster per row; pairs stage half the
+// activation bytes of single CTAs).
+static double tile_row_cost(int bn) {
+    switch (bn) {
+        case -192: return 1.0;
+        case 192: return 1.03;
+        case -128: return 1.36;
+        default: return 1.39;
+    }
+}
+
 static int pick_tile(int N, int m_valid) {
     const int sms = sm_count();
     int best = 128;
@@ -657,8 +671,7 @@ static int pick_tile(int N, int m_valid) {
         const long long rt = (m_valid + w - 1) / w;
         const long long slots = pair ? sms / 2 : sms;
         const long long waves = (ft * rt + slots - 1) / slots;
-        // per-SM time of one tile ~ its rows; pairs stage half the activation bytes
-        const double cost = (double)waves * w * (pair ? 1.0 : 1.08);
+        const double cost = (double)waves * w * tile_row_cost(bn);
         if (cost < best_cost) { best_cost = cost; best = bn; }
     }
     return best;
@@ -679,7 +692,7 @@ static int qgemm_impl(const void* A, long long K, long long M, const void* Bq, c
     if (epilogue < W2V_EPI_F16 || epilogue > W2V_EPI_F32_RESID_LN) return W2V_ERR_ARGS;
     if (M == 0) return W2V_OK;
     const int bn = block_n ? block_n : pick_tile(N, (int)M);
-    if (bn != 192 && bn != 128 && bn != -192 && bn != -128) return W2V_ERR_ARGS;
+    if (bn != 224 && bn != 192 && bn != 128 && bn != -224 && bn != -192 && bn != -128) return W2V_ERR_ARGS;
     const bool pair = bn < 0;
     const int w = pair ? -bn : bn;
     auto enc = get_encode();
