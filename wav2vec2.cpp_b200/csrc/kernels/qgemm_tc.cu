@@ -645,14 +645,16 @@ static int launch_w(int wq, int bn, const CUtensorMap& tx, const CUtensorMap& tq
 }
 
 // Tile: CTA pairs (256 weight rows per tile) or single CTAs (128), each over
-// 192 or 128 activation rows.  Each SM computes 128 weight rows x BN rows per
+// 224, 192 or 128 activation rows.  Each SM computes 128 weight rows x BN rows per
 // tile either way.  Estimated time = waves of tiles over the SMs x tile width
 // x the measured time per activation row of that tile (B200, the base
-// encoder linears at 31936 rows: 192-row tiles stage fewer operand bytes per
-// MAC than 128-row ones, 1.36x faster per row; pairs stage half the
-// activation bytes of single CTAs).
+// encoder linears at 31936 rows: wider tiles stage fewer operand bytes per
+// MAC -- 224 rows 5 % and 192 rows 36 % faster per row than 128 -- and pairs
+// stage half the activation bytes of single CTAs).
 static double tile_row_cost(int bn) {
     switch (bn) {
+        case -224: return 0.95;
+        case 224: return 0.96;
         case -192: return 1.0;
         case 192: return 1.03;
         case -128: return 1.36;
@@ -664,7 +666,7 @@ static int pick_tile(int N, int m_valid) {
     const int sms = sm_count();
     int best = 128;
     double best_cost = 1e300;
-    for (int bn : {-192, -128, 192, 128}) {
+    for (int bn : {-224, -192, -128, 224, 192, 128}) {
         const bool pair = bn < 0;
         const int w = pair ? -bn : bn;
         const long long ft = (N + kRows * (pair ? 2 : 1) - 1) / (kRows * (pair ? 2 : 1));
