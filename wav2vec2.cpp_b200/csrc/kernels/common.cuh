@@ -132,7 +132,7 @@ W2V_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* m, uint64_t* bar, in
         : "memory");
 }
 
-// Tile store shared -> global (no multicast); completion tracked per thread
+// Tile store shared -> global (one destination); completion tracked per thread
 // through bulk async-groups.  Coordinates must be non-negative and the
 // innermost one a multiple of 16 bytes.
 W2V_DEV void tma_store_3d(const CUtensorMap* m, const void* smem_src, int c0, int c1, int c2) {
