@@ -678,6 +678,10 @@ def run_kernel_case(args):
             fn = lambda: K.gemm_ln_resid(A.data_ptr(), Kd, 1, 1, Kd, M, 1, M * Kd, W.data_ptr(), N, out.data_ptr(),
                                          N, M, M, bias.data_ptr(), out.data_ptr(), N, stats.data_ptr(),
                                          lw.data_ptr(), lb.data_ptr(), block_n=args.block_n, stream=st)
+            if args.weights != "f16":
+                fn = lambda: K.gemm_q_ln_resid(A.data_ptr(), Kd, M, codes.data_ptr(), scales.data_ptr(), ld, gt, N,
+                                               out.data_ptr(), N, bias.data_ptr(), out.data_ptr(), N,
+                                               stats.data_ptr(), lw.data_ptr(), lb.data_ptr(), args.block_n, 0, st)
         flops = 2.0 * M * N * Kd
     elif args.kernel == "attention":
         H, nh, T, B = 768, 12, 499, 64

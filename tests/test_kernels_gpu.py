@@ -415,11 +415,13 @@ def test_pos_conv(K, H, G, Kp):
 @pytest.mark.parametrize("H,nh,T", [(768, 12, [499, 1, 64, 65, 200]), (1280, 16, [499, 1, 64, 65, 200]),
                                     (128, 2, [499, 1, 64, 65, 200]), (1024, 8, [499, 1, 64, 65, 200]),
                                     (64, 1, [499, 1, 64, 65, 200]), (768, 12, [1499, 700]),
-                                    (1280, 16, [1499, 33]), (1024, 8, [1499, 257])])
+                                    (1280, 16, [1499, 33]), (1024, 8, [1499, 257]),
+                                    (768, 12, [128, 129, 256, 257, 383, 384, 385, 2, 63])])
 def test_attention(K, H, nh, T):
     """Flash attention vs fp64 softmax(QK^T/sqrt(d))V per utterance
     (src/wav2vec2.cpp:304-334), up to 30 s utterances (T = 1499: 24 key tiles,
-    so the running max is raised mid-sequence)."""
+    so the running max is raised mid-sequence); lengths on either side of
+    the 128-query tile and the 32-key tile boundaries."""
     rng = np.random.default_rng(H + len(T))
     off = np.concatenate([[0], np.cumsum(T)[:-1]]).astype(np.int64)
     M = sum(T)
