@@ -530,7 +530,9 @@ def result_line(args, wl, world, elapsed_ms, audio_timed, prof, steps_prof, laun
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic",
         "config": workload_config(wl, world, lens_rot),
         "roofline": {"bound": "tensor",
-                     "kernel": "gemm_tc_kernel / gemm2_tc_kernel on the encoder linears (tcgen05, TMEM)",
+                     "kernel": ("qgemm_kernel on the encoder linears (dequant-fused tcgen05 GEMM, "
+                                f"{wl.dtype} weights expanded into TMEM)" if wl.dtype in ("q8_0", "q4_0") else
+                                "gemm_tc_kernel / gemm2_tc_kernel on the encoder linears (tcgen05, TMEM)"),
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak if peak else None,
                      "traffic": encoder_gemm_traffic(wl),
@@ -560,12 +562,14 @@ def result_line(args, wl, world, elapsed_ms, audio_timed, prof, steps_prof, laun
 
 
 # DRAM bytes per launch of the four encoder linears of wav2vec2-base at 64 x
-# 499 rows (QKV, attention out-projection + residual, FFN up + GELU, FFN down +
-# residual), from one ncu capture of each on B200 (profiles/gemm_encoder_traffic_b64.md
-# gives the capture, its date and the library build it measured).
-ENCODER_GEMM_DRAM_BYTES = {"qkv": 147.9e6, "out_proj": 188.4e6, "ffn_up": 197.4e6, "ffn_down": 372.5e6}
+# 499 rows on Q8_0 weights through the dequant-fused GEMM (QKV, attention
+# out-projection + LayerNorm residual, FFN up + GELU, FFN down + LayerNorm
+# residual), from one ncu capture of each on B200 (profiles/qgemm_encoder_traffic_b64.md
+# gives the commands and the per-linear figures).
+ENCODER_GEMM_DRAM_BYTES = {"qkv": 146.2e6, "out_proj": 189.2e6, "ffn_up": 194.2e6, "ffn_down": 365.4e6}
 ENCODER_GEMM_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of each encoder "
-                               "linear at 64 x 499 rows, mean per launch (profiles/gemm_encoder_traffic_b64.md)")
+                               "linear through the dequant-fused GEMM on Q8_0 weights at 64 x 499 rows, mean per "
+                               "launch (profiles/qgemm_encoder_traffic_b64.md)")
 
 
 def encoder_gemm_traffic(wl: Workload):
