@@ -178,9 +178,10 @@ int w2v_layer_norm_stats(const float* in, long long M, int D, const float* w, co
  * added to the input.  x: fp32 packed rows [M, H]; utterance u occupies rows
  * off[u] .. off[u]+T[u]; x = xin + gelu(conv(xin) + bias), x != xin.
  * wt: fp16 weights re-laid out by the engine as
- * [G][Kp][Cg/8][Cg (co)][8 (ci within the chunk)], Cg = H/G (one contiguous
- * block of 8-row x 16-byte core matrices per tap); bias fp32 [H].
- * Cg must be 32, 48, 64 or 80; Kp a multiple of 4, at most 128; x, xin, wt
+ * [G][Kp/2][Cg/8][2 Cg][8 (ci within the chunk)], Cg = H/G: per pair of taps
+ * (2p, 2p+1) one contiguous block of 8-row x 16-byte core matrices whose 2 Cg
+ * rows are tap 2p's output channels, then tap 2p+1's; bias fp32 [H].
+ * Cg must be 32, 48, 64 or 80; Kp even, at most 128; x, xin, wt
  * and bias 16-byte aligned.  err: device word for bounded-wait failures. */
 int w2v_pos_conv(float* x, const float* xin, const long long* off, const int* T, int n_utt, int H,
                  int Kp, int G, const void* wt, const float* bias, int max_T, int* err, void* stream);

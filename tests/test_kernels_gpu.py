@@ -384,17 +384,20 @@ def test_layer_norm(K, D, f16in, gelu):
 
 @pytest.mark.parametrize("H,G,Kp", [(768, 16, 128), (128, 4, 16), (1024, 16, 128), (1280, 16, 128)])
 def test_pos_conv(K, H, G, Kp):
-    """Grouped positional conv + GELU + residual (src/wav2vec2.cpp:349-356)."""
+    """Grouped positional conv + GELU + residual (src/wav2vec2.cpp:349-356).
+    Two taps share each MMA and the odd taps' sums land one row early, so a
+    CTA covers 511 frames (383 for 80-channel groups): lengths on both sides
+    of those boundaries and of the 128-frame tiles inside a CTA."""
     rng = np.random.default_rng(H)
-    T = [130, 7, 700, 512]
+    T = [130, 7, 700, 512, 511, 383, 384, 385, 128, 1, 1023]
     off = np.concatenate([[0], np.cumsum(T)[:-1]]).astype(np.int64)
     M = sum(T)
     xin = rng.standard_normal((M, H)).astype(np.float16).astype(np.float32)
     Cg = H // G
     w = (rng.standard_normal((H, Cg, Kp)) * 0.02).astype(np.float16).astype(np.float32)
     b = (rng.standard_normal(H) * 0.1).astype(np.float32)
-    # [G][Kp][Cg/8 (ci chunk)][co][8 (ci)]
-    wt = (w.reshape(G, Cg, Cg // 8, 8, Kp).transpose(0, 4, 2, 1, 3).astype(np.float16).copy())
+    # [G][Kp/2][Cg/8 (ci chunk)][2 Cg (tap parity, co)][8 (ci)]
+    wt = (w.reshape(G, Cg, Cg // 8, 8, Kp // 2, 2).transpose(0, 4, 2, 5, 1, 3).astype(np.float16).copy())
     d_x = torch.full((M, H), float("nan"), device="cuda")
     d_xin, d_off, d_T, d_wt, d_b = dev(xin), dev(off), dev(np.array(T, np.int32)), dev(wt), dev(b)
     err = err_word()

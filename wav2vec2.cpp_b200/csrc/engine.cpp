@@ -144,7 +144,7 @@ ModelConfig ModelConfig::from_gguf(const GgufFile& gf) {
     need(c.pos_g > 0 && c.hidden % c.pos_g == 0, "hidden not divisible by pos_conv_groups");
     const int cg = c.pos_g ? c.hidden / c.pos_g : 0;
     need(cg == 32 || cg == 48 || cg == 64 || cg == 80, "hidden/pos_conv_groups must be 32, 48, 64 or 80");
-    need(c.pos_k > 0 && c.pos_k % 4 == 0 && c.pos_k <= 128, "pos_conv_kernel must be a multiple of 4, at most 128");
+    need(c.pos_k > 0 && c.pos_k % 2 == 0 && c.pos_k <= 128, "pos_conv_kernel must be even, at most 128");
     need(c.conv_k[0] <= 16, "first conv kernel must be <= 16");
     for (int i = 1; i < c.n_conv; i++)
         need(!(c.conv_norm[i] && c.group_norm), "GroupNorm is supported on conv layer 0 only");
@@ -352,8 +352,9 @@ void Engine::load(const GgufFile& gf) {
     upload_floats(proj_lnb_, floats_sized(gf, "feature_projection.layer_norm.bias", C), stream_);
     upload_linears(gf, {"feature_projection.projection"}, {H}, C, proj_w_);
     upload_floats(proj_b_, floats_sized(gf, "feature_projection.projection.bias", H), stream_);
-    // positional conv [H][Cg][Kp] (src/wav2vec2.cpp:211-212) -> per tap, 8-channel
-    // core-matrix blocks: [G][Kp][Cg/8 (ci chunk)][Cg (co)][8 (ci)]
+    // positional conv [H][Cg][Kp] (src/wav2vec2.cpp:211-212) -> per pair of taps
+    // (2p, 2p+1), 8-channel core-matrix blocks with the two taps stacked along
+    // the output channels: [G][Kp/2][Cg/8 (ci chunk)][2 Cg (tap, co)][8 (ci)]
     {
         const int G = c.pos_g, Cg = H / G, Kp = c.pos_k;
         auto w = floats_sized(gf, "encoder.pos_conv_embed.conv.weight", (size_t)H * Cg * Kp);
@@ -362,7 +363,8 @@ void Engine::load(const GgufFile& gf) {
             for (int oc = 0; oc < Cg; oc++)
                 for (int ic = 0; ic < Cg; ic++)
                     for (int k = 0; k < Kp; k++)
-                        r[((((size_t)g * Kp + k) * (Cg / 8) + ic / 8) * Cg + oc) * 8 + ic % 8] =
+                        r[((((size_t)g * (Kp / 2) + k / 2) * (Cg / 8) + ic / 8) * (2 * Cg) + (k % 2) * Cg + oc) * 8 +
+                          ic % 8] =
                             w[((size_t)(g * Cg + oc) * Cg + ic) * Kp + k];
         upload_f16(pos_w_, r, stream_);
         upload_floats(pos_b_, floats_sized(gf, "encoder.pos_conv_embed.conv.bias", H), stream_);
