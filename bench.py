@@ -644,7 +644,8 @@ def run_kernel_case(args):
     gemm: M rows x K -> N with the given epilogue (default the encoder FFN-up
           shape, K=768 -> N=3072, fp16 out, GELU epilogue);
     attention: 64 utterances x 499 frames, 12 heads x 64;
-    pos_conv: the same batch, hidden 768, kernel 128, 16 groups."""
+    pos_conv: the same batch, hidden 768, kernel 128, 16 groups;
+    layer_norm: M rows of 768 (fp32 in, fp16 + row statistics out)."""
     import torch
     pkg()
     import w2v_b200.binding as b
@@ -695,6 +696,17 @@ def run_kernel_case(args):
         Tt = torch.full((B,), T, device="cuda", dtype=torch.int32)
         fn = lambda: K.attention(qkv.data_ptr(), out.data_ptr(), off.data_ptr(), Tt.data_ptr(), B, H, nh, T, B * T, 0, st)
         flops = 4.0 * B * T * T * H
+    elif args.kernel == "layer_norm":
+        # post-LN encoder LayerNorm: fp32 rows in, fp16 normalised rows + (mean, rstd) out
+        H, M = 768, args.rows
+        x = torch.randn(M, H, device="cuda")
+        xh = torch.empty(M, H, device="cuda", dtype=torch.float16)
+        stats = torch.empty(M, 2, device="cuda")
+        lw, lb = torch.randn(H, device="cuda"), torch.randn(H, device="cuda")
+        fn = lambda: K.layer_norm_stats(x.data_ptr(), M, H, lw.data_ptr(), lb.data_ptr(), xh.data_ptr(),
+                                        stats.data_ptr(), st)
+        flops = 0.0
+        nbytes = M * H * (4 + 2) + M * 8
     else:
         H, G, Kp, T, B = 768, 16, 128, 499, 64
         x = torch.randn(B * T, H, device="cuda")
@@ -717,6 +729,8 @@ def run_kernel_case(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     rec = {"kernel": args.kernel, "rows": M, "ms": ms, "tflops": flops / ms / 1e9}
+    if args.kernel == "layer_norm":
+        rec = {"kernel": args.kernel, "rows": M, "ms": ms, "gbs": nbytes / ms / 1e6}
     if args.kernel == "gemm":
         rec.update(shape=args.gemm_shape, block_n=args.block_n, weights=args.weights)
     print(json.dumps(rec), flush=True)
@@ -738,7 +752,7 @@ def main():
                     help="seconds of the all-cores reference throughput sample")
     ap.add_argument("--ref-budget", type=float, default=150.0, help="seconds for the --impl reference CLI calls")
     ap.add_argument("--cache", default=os.environ.get("W2V_MODEL_CACHE", "/tmp/w2v_models"))
-    ap.add_argument("--kernel", choices=["gemm", "attention", "pos_conv"], default=None,
+    ap.add_argument("--kernel", choices=["gemm", "attention", "pos_conv", "layer_norm"], default=None,
                     help="time one kernel at a representative size instead of the whole step")
     ap.add_argument("--rows", type=int, default=32768, help="GEMM rows for --kernel gemm")
     ap.add_argument("--gemm-shape", default="3072,768,1",

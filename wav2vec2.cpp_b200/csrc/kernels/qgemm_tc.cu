@@ -64,14 +64,23 @@ struct QParams {
     int* err;
 };
 
-template <int BN, int WQ, bool PAIR>
+template <int BN, int WQ, bool PAIR, int EPI>
 struct QCfg {
     static constexpr int kXRows = PAIR ? BN / 2 : BN;          // activation rows one CTA stages
     static constexpr int kXBytes = kXRows * kBK * 2;
     static constexpr int kCodeBytes = kRows * code_row_bytes(WQ);
     static constexpr int kScaleBytes = 2 * kRows * 2;
     static constexpr int kPer = kXBytes + kCodeBytes + kScaleBytes;
-    static constexpr int kEpiBytes = kNE * 16384;   // per epilogue warp: two output and two residual boxes
+    // Staged epilogue, per epilogue warp: two 32 x 32 output boxes (fp16 or fp32),
+    // and for the residual epilogues a ring of kResBoxes fp32 residual boxes
+    // (fetched kResBoxes - 1 chunks ahead: the residual does not depend on the
+    // MMA, and one box ahead left every chunk waiting on a DRAM round trip);
+    // then per warp the current chunk's row statistics (256 B).
+    static constexpr bool kRes = EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN;
+    static constexpr int kOutBox = (EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU) ? 2048 : 4096;
+    static constexpr int kResBoxes = kRes ? 4 : 0;
+    static constexpr int kEpiWarp = 2 * kOutBox + kResBoxes * 4096;
+    static constexpr int kEpiBytes = kNE * (kEpiWarp + 256);
     static constexpr int kStages = cmin(8, (kSmemCap - 1024 - 512 - kEpiBytes) / kPer);
     static constexpr int kOffCode = kStages * kXBytes;
     static constexpr int kOffScale = kOffCode + kStages * kCodeBytes;
@@ -82,6 +91,7 @@ struct QCfg {
     static constexpr int kACol = 2 * BN;                        // first weight-tile column
     static_assert(kStages >= 2 && kSB >= 2, "plan");
     static_assert(kXBytes % 1024 == 0 && kCodeBytes % 1024 == 0, "alignment");
+    static_assert((3 * kStages + 2 * kSB + 5 + kNE * (kResBoxes > 2 ? kResBoxes : 2)) * 8 + 4 <= 512, "barriers");
 };
 
 // ── tcgen05 forms used only here ────────────────────────────────────────────
@@ -140,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmQ,
              const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmC,
              const __grid_constant__ CUtensorMap tmR, QParams p) {
-    using Cfg = QCfg<BN, WQ, PAIR>;
+    using Cfg = QCfg<BN, WQ, PAIR, EPI>;
     constexpr int S = Cfg::kStages, SB = Cfg::kSB, CT = PAIR ? 2 : 1;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -157,8 +167,9 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
     uint64_t* tfull = aempty + SB;         // accumulator b ready (each CTA)
     uint64_t* tempty = tfull + 2;          // accumulator b drained (pair: leader, both CTAs' epilogues)
     uint64_t* done = tempty + 2;
-    uint64_t* rbar = done + 1;             // residual box b of epilogue warp w landed: rbar[2 w + b]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2 * kNE);
+    constexpr int RB = Cfg::kResBoxes > 0 ? Cfg::kResBoxes : 1;
+    uint64_t* rbar = done + 1;             // residual box b of epilogue warp w landed: rbar[RB w + b]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + RB * kNE);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
@@ -171,7 +182,7 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
         for (int f = 0; f < SB; f++) { mbar_init(&afull[f], kNC * CT); mbar_init(&aempty[f], 1); }
         for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], kNE * CT); }
         mbar_init(done, 1);
-        for (int i = 0; i < 2 * kNE; i++) mbar_init(&rbar[i], 1);
+        for (int i = 0; i < RB * kNE; i++) mbar_init(&rbar[i], 1);
         fence_mbar_init();
         tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmQ);
@@ -345,17 +356,21 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
         // epilogue: lane = output feature, the 32 registers of a chunk = 32 activation rows
         const int q = warp & 3;
         if (p.tma) {
-            // Staged: per 32 x 32 chunk, the residual box arrives by TMA one chunk
-            // ahead (two boxes per warp), and the results go through one of two
-            // output boxes and a TMA tile store.  Register j of lane f is row j,
+            // Staged: per 32 x 32 chunk, the residual box arrives by TMA R - 1 chunks
+            // ahead (a ring of R boxes per warp, the first R - 1 requested before the
+            // accumulator is ready), and the results go through one of two output
+            // boxes and a TMA tile store.  Register j of lane f is row j,
             // feature f of the box: each shared-memory access of the warp touches
             // one contiguous 64- or 128-byte box row, so none conflicts on a bank.
             constexpr bool kRes = EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN;
             constexpr bool kF16 = EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU;
             constexpr int kNch = BN / 32;
-            uint8_t* ebase = smem + Cfg::kOffEpi + (warp - 2) * 16384;
-            float* rbox = reinterpret_cast<float*>(ebase + 8192);
-            uint64_t* rb = rbar + 2 * (warp - 2);
+            constexpr uint32_t R = RB;             // residual boxes per warp (residual epilogues)
+            uint8_t* ebase = smem + Cfg::kOffEpi + (warp - 2) * Cfg::kEpiWarp;
+            float* rbox = reinterpret_cast<float*>(ebase + 2 * Cfg::kOutBox);
+            // rows 2i, 2i+1 of the chunk: (mean, rstd, mean, rstd)
+            float4* sst = reinterpret_cast<float4*>(smem + Cfg::kOffEpi + kNE * Cfg::kEpiWarp + (warp - 2) * 256);
+            uint64_t* rb = rbar + RB * (warp - 2);
             const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : 0u;
             uint32_t nst = 0, nrl = 0, nrw = 0;   // output boxes stored, residual boxes requested / awaited
             int it = 0;
@@ -383,15 +398,19 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                     continue;
                 }
                 auto request = [&](int c) {          // residual box of chunk c (lane 0)
-                    const uint32_t b = nrl & 1u;
+                    const uint32_t b = nrl % R;
                     fence_async_smem();              // earlier reads of this box precede the TMA write
                     mbar_arrive_expect_tx(&rb[b], 32 * 32 * 4);
                     tma_load_2d(rbox + b * 1024, &tmR, &rb[b], fcol0, ri * BN + c * 32);
                 };
                 const uint32_t rfirst = nrl;
+                int nreq = 0;                        // chunks of this tile whose residual is requested
                 if constexpr (kRes) {
-                    if (lane == 0) request(0);
-                    nrl++;
+                    // chunks 0 .. R-2 before the accumulator is ready; chunk c + R - 1 at chunk c
+                    for (; nreq < (int)R - 1 && nreq < kNch && ri * BN + nreq * 32 < p.m_valid; nreq++) {
+                        if (lane == 0) request(nreq);
+                        nrl++;
+                    }
                 }
                 float2 stn = make_float2(0.f, 0.f);
                 if (EPI == W2V_EPI_F32_RESID_LN && ri * BN + lane < p.m_valid) stn = p.ln_stats[ri * BN + lane];
@@ -419,17 +438,23 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                     const float* rcur = rbox;
                     if constexpr (kRes) {
                         const uint32_t idx = rfirst + (uint32_t)c;
-                        if (c + 1 < kNch && r0 + 32 < p.m_valid) {
-                            __syncwarp();            // every lane is done with the box chunk c+1 reuses
-                            if (lane == 0) request(c + 1);
+                        if (nreq < kNch && ri * BN + nreq * 32 < p.m_valid) {
+                            __syncwarp();            // every lane is done with the box chunk nreq reuses (chunk c - 1's)
+                            if (lane == 0) request(nreq);
                             nrl++;
+                            nreq++;
                         }
-                        if (!mbar_wait(&rb[idx & 1u], (idx >> 1) & 1u, p.err)) { ok = false; break; }
+                        if (!mbar_wait(&rb[idx % R], (idx / R) & 1u, p.err)) { ok = false; break; }
                         nrw = idx + 1;
-                        rcur = rbox + (idx & 1u) * 1024;
+                        rcur = rbox + (idx % R) * 1024;
                     }
-                    uint8_t* ob = ebase + (nst & 1u) * 4096;
+                    uint8_t* ob = ebase + (nst & 1u) * Cfg::kOutBox;
                     if (lane == 0) bulk_wait_group_read<1>();   // the store issued from this box two boxes ago has read it
+                    if (EPI == W2V_EPI_F32_RESID_LN) {
+                        // the chunk's row statistics, read back by every lane as a broadcast
+                        // (the previous chunk's reads precede this store: __syncwarp above)
+                        reinterpret_cast<float2*>(sst)[lane] = st;
+                    }
                     __syncwarp();
                     if constexpr (kF16) {
                         __half* oh = reinterpret_cast<__half*>(ob);
@@ -443,14 +468,19 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                     } else {
                         float* of = reinterpret_cast<float*>(ob);
 #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            float a = v[j] + bias;
-                            if (EPI == W2V_EPI_F32_RESID) a += rcur[j * 32 + lane];
-                            if (EPI == W2V_EPI_F32_RESID_LN) {
-                                const float m = __shfl_sync(0xffffffffu, st.x, j), sd = __shfl_sync(0xffffffffu, st.y, j);
-                                a += (rcur[j * 32 + lane] - m) * sd * lw + lb;
+                        for (int j = 0; j < 32; j += 2) {
+                            float a0 = v[j] + bias, a1 = v[j + 1] + bias;
+                            if (EPI == W2V_EPI_F32_RESID) {
+                                a0 += rcur[j * 32 + lane];
+                                a1 += rcur[(j + 1) * 32 + lane];
                             }
-                            of[j * 32 + lane] = a;
+                            if (EPI == W2V_EPI_F32_RESID_LN) {
+                                const float4 s2 = sst[j / 2];
+                                a0 += (rcur[j * 32 + lane] - s2.x) * s2.y * lw + lb;
+                                a1 += (rcur[(j + 1) * 32 + lane] - s2.z) * s2.w * lw + lb;
+                            }
+                            of[j * 32 + lane] = a0;
+                            of[(j + 1) * 32 + lane] = a1;
                         }
                     }
                     fence_async_smem();
@@ -465,7 +495,8 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
             }
             // the stores have completed and no residual box is still being written
             // (after an expired wait boxes may have been requested and not awaited)
-            for (uint32_t idx = nrw; idx < nrl; idx++) mbar_wait(&rb[idx & 1u], (idx >> 1) & 1u, p.err);
+            if constexpr (kRes)
+                for (uint32_t idx = nrw; idx < nrl; idx++) mbar_wait(&rb[idx % R], (idx / R) & 1u, p.err);
             if (lane == 0) bulk_wait_group<0>();
             __syncwarp();
         } else {
@@ -587,7 +618,7 @@ static int sm_count() {
 template <int BN, int EPI, int WQ, bool PAIR>
 static int launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts, const CUtensorMap& tc,
                   const CUtensorMap& tr, const QParams& p, cudaStream_t st) {
-    using Cfg = QCfg<BN, WQ, PAIR>;
+    using Cfg = QCfg<BN, WQ, PAIR, EPI>;
     auto kern = qgemm_kernel<BN, EPI, WQ, PAIR>;
     static int max_units[64] = {};
     int dev = 0;
