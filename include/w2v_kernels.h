@@ -81,8 +81,8 @@ int w2v_gemm_f16_ln_resid(const void* A, long long a_cin, int a_taps, int a_stri
  * src/ggml_backend.h:78-120).  A: fp16 [M, K] activation rows (K % 64 == 0);
  * C, bias, resid and the epilogues as w2v_gemm_f16 (not
  * W2V_EPI_F32_RESID_LN: w2v_gemm_q_ln_resid).  block_n: 0 = automatic,
- * 128/192 = one CTA per 128 weight rows x block_n activation rows,
- * -128/-192 = a CTA pair per 256 weight rows x -block_n activation rows. */
+ * 64/128/192/224 = one CTA per 128 weight rows x block_n activation rows,
+ * -128/-192/-224 = a CTA pair per 256 weight rows x -block_n activation rows. */
 int w2v_gemm_q(const void* A, long long K, long long M, const void* Bq, const void* Bs, long long ld_s,
                int gguf_type, int N, void* C, long long ldc, const float* bias, const float* resid,
                long long ldr, int epilogue, int block_n, int* err, void* stream);

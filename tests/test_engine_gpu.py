@@ -230,6 +230,50 @@ def test_forward_device_outputs(W, model_path, synth):
     assert ns.tolist() == [len(O.greedy_spans(r)) for r in ref]
 
 
+def test_forward_device_graph_replays_equal_eager(W, model_path, synth, monkeypatch):
+    """Engine::forward captures the forward of a (device input, lengths) pair
+    the second time it sees it and replays the CUDA graph afterwards.  Every
+    call -- eager, capture, replays, a replay over new audio at the same
+    address, a new geometry -- gives the logits of a model that never captures
+    (W2V_B200_GRAPHS=0), bit for bit, with the same launch count."""
+    p = model_path("base", "q8_0")
+    m = W.Model(p)
+    monkeypatch.setenv("W2V_B200_GRAPHS", "0")
+    me = W.Model(p)
+    monkeypatch.delenv("W2V_B200_GRAPHS")
+    V = m.cfg["vocab"]
+    s = torch.cuda.Stream()
+
+    def run(model, d, lens):
+        with torch.cuda.stream(s):
+            model.forward_device(d.data_ptr(), lens, s.cuda_stream)
+        s.synchronize()
+        lg_ptr, _, _, M = model.device_outputs()
+        return torch.as_tensor(_DevArray(lg_ptr, M * V, "<f4"), device="cuda").cpu().numpy().copy()
+
+    lens = [16000, 31234]
+    d = torch.from_numpy(np.concatenate([synth.make_audio(n, 70 + i) for i, n in enumerate(lens)])).cuda()
+    ref = run(me, d, lens)
+    n_eager = me.launches_per_forward()
+    for _ in range(4):
+        assert np.array_equal(run(m, d, lens), ref)
+        assert m.launches_per_forward() == n_eager
+    # same address, new samples: the replay reads them
+    d.copy_(torch.from_numpy(np.concatenate([synth.make_audio(n, 90 + i) for i, n in enumerate(lens)])))
+    ref2 = run(me, d, lens)
+    assert not np.array_equal(ref2, ref)
+    assert np.array_equal(run(m, d, lens), ref2)
+    # another geometry (and a larger workspace: earlier captures are dropped)
+    lens3 = [48000, 16000, 20000]
+    d3 = torch.from_numpy(np.concatenate([synth.make_audio(n, 110 + i) for i, n in enumerate(lens3)])).cuda()
+    ref3 = run(me, d3, lens3)
+    for _ in range(3):
+        assert np.array_equal(run(m, d3, lens3), ref3)
+    assert np.array_equal(run(m, d, lens), ref2)
+    m.close()
+    me.close()
+
+
 def test_init_rejects_bad_model(W, tmp_path):
     bad = tmp_path / "bad.gguf"
     bad.write_bytes(b"GGUF" + b"\0" * 10)

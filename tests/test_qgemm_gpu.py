@@ -107,10 +107,11 @@ def run_pair(K, q, M, epi, bn, seed):
     (499, 3072, 768, EPI_F16_GELU, 0), (499, 32, 768, EPI_F32, 0), (1, 128, 64, EPI_F32, 128),
     (31936, 2304, 768, EPI_F16, -192), (5000, 768, 3072, EPI_F32_RESID, -192), (777, 1024, 1024, EPI_F32, 128),
     (300, 768, 768, EPI_F32_RESID, -128), (2049, 200, 512, EPI_F16, 192), (130, 96, 256, EPI_F16_GELU, -128),
-    (4000, 3072, 768, EPI_F16_GELU, 0), (3001, 768, 768, EPI_F32_RESID, -224), (700, 320, 512, EPI_F16, 224)])
+    (4000, 3072, 768, EPI_F16_GELU, 0), (3001, 768, 768, EPI_F32_RESID, -224), (700, 320, 512, EPI_F16, 224),
+    (499, 2304, 768, EPI_F16, 64), (499, 768, 3072, EPI_F32_RESID, 64), (77, 200, 256, EPI_F32, 64)])
 def test_gemm_q_matches_fp16_gemm(K, synth, gtype, M, N, Kd, epi, bn):
-    """Every tile family (CTA pairs and single CTAs, 192 and 128 activation
-    rows), ragged rows and features, every epilogue."""
+    """Every tile family (CTA pairs and single CTAs, 224, 192, 128 and 64
+    activation rows), ragged rows and features, every epilogue."""
     q = QLinear(K, synth, N, Kd, gtype, M + N)
     out_q, out_f, ref, f16 = run_pair(K, q, M, epi, bn, M * 3 + N)
     assert torch.isfinite(out_q).all()
@@ -124,7 +125,7 @@ def test_gemm_q_matches_fp16_gemm(K, synth, gtype, M, N, Kd, epi, bn):
         assert (d <= 2e-5 * (1 + out_f.double().abs())).all(), d.max().item()
 
 
-@pytest.mark.parametrize("gtype,bn", [(Q8_0, -192), (Q4_0, -128), (Q8_0, 128)])
+@pytest.mark.parametrize("gtype,bn", [(Q8_0, -192), (Q4_0, -128), (Q8_0, 128), (Q8_0, 64), (Q4_0, -224)])
 def test_gemm_q_ln_resid(K, synth, gtype, bn):
     """Post-LN residual epilogue (the residual normalised on the fly from
     per-row statistics), in place over C."""

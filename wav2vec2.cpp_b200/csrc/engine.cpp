@@ -163,11 +163,12 @@ int ModelConfig::frames(long long n) const {
 
 // ── device buffers ──────────────────────────────────────────────────────────
 
-void DevBuf::ensure(size_t bytes) {
-    if (bytes <= n) return;
+bool DevBuf::ensure(size_t bytes) {
+    if (bytes <= n) return false;
     release();
     cuda_check(cudaMalloc(&p, bytes), "cudaMalloc");
     n = bytes;
+    return true;
 }
 void DevBuf::release() {
     if (p) cudaFree(p);
@@ -186,6 +187,7 @@ Engine::Engine(const GgufFile& gf, const ModelConfig& cfg, int device) : cfg_(cf
     cuda_check(cudaEventCreate(&busy0_), "cudaEventCreate");
     cuda_check(cudaEventCreate(&busy1_), "cudaEventCreate");
     if (const char* e = getenv("W2V_B200_EXPAND_WEIGHTS")) expand_weights_ = atoi(e) != 0;
+    if (const char* e = getenv("W2V_B200_GRAPHS")) graphs_enabled_ = atoi(e) != 0;
     err_.ensure(sizeof(int));
     // Every transfer of the engine is ordered on its own (non-blocking) stream:
     // a legacy-stream cudaMemcpy from pageable memory may return before its DMA
@@ -199,6 +201,8 @@ Engine::~Engine() {
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
     if (copy_stream_) cudaStreamSynchronize(copy_stream_);
+    cudaDeviceSynchronize();   // replays of captured forwards may run on caller streams
+    drop_graphs();
     auto rel = [](DevBuf& b) { b.release(); };
     for (DevBuf* b : {&conv0_w_, &conv0_b_, &proj_lnw_, &proj_lnb_, &proj_w_.w, &proj_w_.s, &proj_b_, &pos_w_, &pos_b_,
                       &enc_lnw_, &enc_lnb_, &lm_w_.w, &lm_w_.s, &lm_b_, &audio_stage_, &meta_, &stats_, &gn_, &actA_,
@@ -449,24 +453,36 @@ void Engine::ensure_workspace(const BatchGeom& g) {
         size_t& a = (i % 2) ? a1 : a0;
         a = std::max<size_t>(a, B * (size_t)g.R[i] * C * 2);
     }
-    actA_.ensure(std::max<size_t>(a0, 16));
-    actB_.ensure(std::max<size_t>(a1, 16));
-    stats_.ensure(B * 2 * sizeof(float));
-    gn_.ensure(B * C * 2 * sizeof(double));
-    feat_.ensure(M * C * 2);
-    pbuf_.ensure(M * H * 4);
-    x_.ensure(M * H * 4);
-    ybuf_.ensure(M * H * 4);
-    lnstats_.ensure(M * 2 * sizeof(float));
-    xh_.ensure(M * H * 2);
-    attn_.ensure(M * H * 2);
-    qkv_.ensure(M * 3 * H * 2);
-    hbuf_.ensure(M * F * 2);
-    logits_.ensure(M * V * 4);
-    ids_.ensure(M * 4);
-    spans_.ensure(M * 3 * 4);
-    nspans_.ensure(B * 4);
-    meta_.ensure(B * (8 + 8 + 4 + 4 + 4 * (size_t)c.n_conv) + 64);
+    bool re = false;
+    re |= actA_.ensure(std::max<size_t>(a0, 16));
+    re |= actB_.ensure(std::max<size_t>(a1, 16));
+    re |= stats_.ensure(B * 2 * sizeof(float));
+    re |= gn_.ensure(B * C * 2 * sizeof(double));
+    re |= feat_.ensure(M * C * 2);
+    re |= pbuf_.ensure(M * H * 4);
+    re |= x_.ensure(M * H * 4);
+    re |= ybuf_.ensure(M * H * 4);
+    re |= lnstats_.ensure(M * 2 * sizeof(float));
+    re |= xh_.ensure(M * H * 2);
+    re |= attn_.ensure(M * H * 2);
+    re |= qkv_.ensure(M * 3 * H * 2);
+    re |= hbuf_.ensure(M * F * 2);
+    re |= logits_.ensure(M * V * 4);
+    re |= ids_.ensure(M * 4);
+    re |= spans_.ensure(M * 3 * 4);
+    re |= nspans_.ensure(B * 4);
+    re |= meta_.ensure(B * (8 + 8 + 4 + 4 + 4 * (size_t)c.n_conv) + 64);
+    if (re) {
+        // captured forwards hold the old buffers' addresses
+        ws_gen_++;
+        drop_graphs();
+    }
+}
+
+void Engine::drop_graphs() {
+    for (auto& e : graphs_) cudaGraphExecDestroy(e.exec);
+    graphs_.clear();
+    graph_seen_.clear();
 }
 
 void Engine::upload_meta(const BatchGeom& g, cudaStream_t st) {
@@ -695,7 +711,46 @@ void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, fl
 
 void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, float* dbg_feat, float* dbg_stages) {
     if (!st) st = stream_;
-    if (!fwd_begin(g, st)) return;
+    if (!fwd_begin(g, st)) return;   // workspace and metadata upload: never part of a captured graph
+    if (graphs_enabled_ && !profiling_ && !dbg_feat && !dbg_stages) {
+        // Replay a captured forward of this (input, lengths): one launch instead
+        // of about a hundred, which is what a single short utterance waits on.
+        for (auto& e : graphs_)
+            if (e.audio == d_audio && e.ws_gen == ws_gen_ && e.n_samples == g.n_samples) {
+                cuda_check(cudaGraphLaunch(e.exec, st), "cudaGraphLaunch");
+                launches_last_ = e.launches;
+                return;
+            }
+        bool seen = false;
+        for (auto& k : graph_seen_)
+            if (k.first == d_audio && k.second == g.n_samples) seen = true;
+        if (seen) {
+            cudaGraph_t graph = nullptr;
+            cuda_check(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+            try {
+                fwd_extract(d_audio, g, 0, g.n_utt, st);
+                fwd_encode(g, st, nullptr, nullptr);
+            } catch (...) {
+                cudaStreamEndCapture(st, &graph);
+                if (graph) cudaGraphDestroy(graph);
+                throw;
+            }
+            cuda_check(cudaStreamEndCapture(st, &graph), "cudaStreamEndCapture");
+            cudaGraphExec_t exec = nullptr;
+            const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            cuda_check(ie, "cudaGraphInstantiate");
+            if (graphs_.size() >= 8) {
+                cudaGraphExecDestroy(graphs_.front().exec);
+                graphs_.erase(graphs_.begin());
+            }
+            graphs_.push_back({d_audio, g.n_samples, ws_gen_, exec, launches_last_});
+            cuda_check(cudaGraphLaunch(exec, st), "cudaGraphLaunch");
+            return;
+        }
+        if (graph_seen_.size() >= 16) graph_seen_.erase(graph_seen_.begin());
+        graph_seen_.push_back({d_audio, g.n_samples});
+    }
     fwd_extract(d_audio, g, 0, g.n_utt, st);
     fwd_encode(g, st, dbg_feat, dbg_stages);
 }

@@ -37,7 +37,7 @@ struct ModelConfig {
 struct DevBuf {
     void* p = nullptr;
     size_t n = 0;
-    void ensure(size_t bytes);
+    bool ensure(size_t bytes);   // true if the buffer was (re)allocated
     void release();
     template <typename T> T* as() const { return static_cast<T*>(p); }
 };
@@ -173,6 +173,23 @@ private:
     DevBuf err_;
     long long last_M_ = 0;
     long long launches_cur_ = 0, launches_last_ = 0;
+
+    // Captured forwards (CUDA graphs) of Engine::forward, keyed by the input
+    // pointer and the utterance lengths; valid while no workspace buffer is
+    // reallocated (ws_gen_).  A geometry is captured the second time it is
+    // seen, so one-off batches and the first call's lazy set-up run eagerly.
+    struct GraphEntry {
+        const float* audio;
+        std::vector<int> n_samples;
+        uint64_t ws_gen;
+        cudaGraphExec_t exec;
+        long long launches;
+    };
+    std::vector<GraphEntry> graphs_;
+    std::vector<std::pair<const float*, std::vector<int>>> graph_seen_;
+    uint64_t ws_gen_ = 0;
+    bool graphs_enabled_ = true;   // W2V_B200_GRAPHS=0: always launch kernel by kernel
+    void drop_graphs();
 
     struct ProfRec { int cat; cudaEvent_t a, b; double flops; };
     bool profiling_ = false;

@@ -664,6 +664,7 @@ static int launch_tile(int bn, const CUtensorMap& tx, const CUtensorMap& tq, con
         case -128: return launch<128, EPI, WQ, true>(tx, tq, ts, tc, tr, p, st);
         case 192: return launch<192, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
         case 128: return launch<128, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
+        case 64: return launch<64, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
         default: return W2V_ERR_ARGS;
     }
 }
@@ -676,12 +677,15 @@ static int launch_w(int wq, int bn, const CUtensorMap& tx, const CUtensorMap& tq
 }
 
 // Tile: CTA pairs (256 weight rows per tile) or single CTAs (128), each over
-// 224, 192 or 128 activation rows.  Each SM computes 128 weight rows x BN rows per
-// tile either way.  Estimated time = waves of tiles over the SMs x tile width
-// x the measured time per activation row of that tile (B200, the base
-// encoder linears at 31936 rows: wider tiles stage fewer operand bytes per
-// MAC -- 224 rows 5 % and 192 rows 36 % faster per row than 128 -- and pairs
-// stage half the activation bytes of single CTAs).
+// 224, 192 or 128 activation rows, or single CTAs over 64 rows for short
+// batches.  Each SM computes 128 weight rows x BN rows per tile either way.
+// Estimated time = waves of tiles over the SMs x tile width x the measured
+// time per activation row of that tile (B200, the base encoder linears at
+// 31936 rows: wider tiles stage fewer operand bytes per MAC -- 224 rows 5 %
+// and 192 rows 36 % faster per row than 128 -- and pairs stage half the
+// activation bytes of single CTAs; 64 rows expand each weight k-block for
+// half as many rows as 128).  Short batches (one utterance: 499 rows) fill
+// more SMs with 64-row tiles.
 static double tile_row_cost(int bn) {
     switch (bn) {
         case -224: return 0.95;
@@ -689,7 +693,8 @@ static double tile_row_cost(int bn) {
         case -192: return 1.0;
         case 192: return 1.03;
         case -128: return 1.36;
-        default: return 1.39;
+        case 128: return 1.39;
+        default: return 2.2;
     }
 }
 
@@ -697,7 +702,7 @@ static int pick_tile(int N, int m_valid) {
     const int sms = sm_count();
     int best = 128;
     double best_cost = 1e300;
-    for (int bn : {-224, -192, -128, 224, 192, 128}) {
+    for (int bn : {-224, -192, -128, 224, 192, 128, 64}) {
         const bool pair = bn < 0;
         const int w = pair ? -bn : bn;
         const long long ft = (N + kRows * (pair ? 2 : 1) - 1) / (kRows * (pair ? 2 : 1));
@@ -725,7 +730,7 @@ static int qgemm_impl(const void* A, long long K, long long M, const void* Bq, c
     if (epilogue < W2V_EPI_F16 || epilogue > W2V_EPI_F32_RESID_LN) return W2V_ERR_ARGS;
     if (M == 0) return W2V_OK;
     const int bn = block_n ? block_n : pick_tile(N, (int)M);
-    if (bn != 224 && bn != 192 && bn != 128 && bn != -224 && bn != -192 && bn != -128) return W2V_ERR_ARGS;
+    if (bn != 224 && bn != 192 && bn != 128 && bn != 64 && bn != -224 && bn != -192 && bn != -128) return W2V_ERR_ARGS;
     const bool pair = bn < 0;
     const int w = pair ? -bn : bn;
     auto enc = get_encode();
