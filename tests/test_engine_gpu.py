@@ -274,6 +274,29 @@ def test_forward_device_graph_replays_equal_eager(W, model_path, synth, monkeypa
     me.close()
 
 
+def test_host_path_graph_replays_equal_eager(W, model_path, synth, monkeypatch):
+    """Host batches of fewer than 8 utterances upload in one piece and then
+    run the forward through the same capture/replay cache: repeated calls
+    (pageable and page-locked inputs, one utterance and a ragged five) give
+    the logits of a model that never captures, bit for bit."""
+    p = model_path("base", "q8_0")
+    m = W.Model(p)
+    monkeypatch.setenv("W2V_B200_GRAPHS", "0")
+    me = W.Model(p)
+    monkeypatch.delenv("W2V_B200_GRAPHS")
+    one = [synth.make_audio(160000, 130)]
+    five = [synth.make_audio(n, 140 + i) for i, n in enumerate([16000, 48000, 33333, 8000, 20000])]
+    keep = [torch.from_numpy(x).pin_memory() for x in five]
+    pinned = [t.numpy() for t in keep]
+    for batch in (one, five, pinned):
+        ref = me.logits(batch)
+        for _ in range(4):
+            got = m.logits(batch)
+            assert all(np.array_equal(a, b) for a, b in zip(got, ref))
+    m.close()
+    me.close()
+
+
 def test_init_rejects_bad_model(W, tmp_path):
     bad = tmp_path / "bad.gguf"
     bad.write_bytes(b"GGUF" + b"\0" * 10)

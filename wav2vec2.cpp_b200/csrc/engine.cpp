@@ -712,6 +712,11 @@ void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, fl
 void Engine::forward(const float* d_audio, const BatchGeom& g, cudaStream_t st, float* dbg_feat, float* dbg_stages) {
     if (!st) st = stream_;
     if (!fwd_begin(g, st)) return;   // workspace and metadata upload: never part of a captured graph
+    extract_encode(d_audio, g, st, dbg_feat, dbg_stages);
+}
+
+void Engine::extract_encode(const float* d_audio, const BatchGeom& g, cudaStream_t st, float* dbg_feat,
+                            float* dbg_stages) {
     if (graphs_enabled_ && !profiling_ && !dbg_feat && !dbg_stages) {
         // Replay a captured forward of this (input, lengths): one launch instead
         // of about a hundred, which is what a single short utterance waits on.
@@ -813,7 +818,36 @@ void Engine::run_host(const std::vector<const float*>& audio, const std::vector<
     // device span of this batch: from before its first upload (copy stream)
     // to after its last download (compute stream)
     cuda_check(cudaEventRecord(busy0_, copy_stream_), "busy event");
-    if (pinned && fwd_begin(g, stream_)) {
+    if (nch == 1 && fwd_begin(g, stream_)) {
+        // one chunk (short batches): upload, then the whole forward, which
+        // repeated batches of the same lengths replay as one captured graph
+        if (pinned) {
+            for (int u = 0; u < B; u++)
+                if (n_samples[u])
+                    cuda_check(cudaMemcpyAsync(audio_stage_.as<float>() + g.audio_off[u], audio[u],
+                                               (size_t)n_samples[u] * sizeof(float), cudaMemcpyHostToDevice,
+                                               copy_stream_),
+                               "audio upload");
+        } else {
+            std::vector<std::thread> packers;
+            struct Joiner {
+                std::vector<std::thread>& v;
+                ~Joiner() {
+                    for (auto& t : v)
+                        if (t.joinable()) t.join();
+                }
+            } joiner{packers};
+            for (int t = 0; t < nt; t++) packers.emplace_back(pack, t);
+            for (auto& t : packers) t.join();
+            if (total)
+                cuda_check(cudaMemcpyAsync(audio_stage_.as<float>(), h_audio_, total * sizeof(float),
+                                           cudaMemcpyHostToDevice, copy_stream_),
+                           "audio upload");
+        }
+        cuda_check(cudaEventRecord(chunk_ev_[0], copy_stream_), "chunk event");
+        cuda_check(cudaStreamWaitEvent(stream_, chunk_ev_[0], 0), "chunk wait");
+        extract_encode(audio_stage_.as<float>(), g, stream_, nullptr, nullptr);
+    } else if (pinned && fwd_begin(g, stream_)) {
         for (int k = 0; k < nch; k++) {
             for (int u = cu[k]; u < cu[k + 1]; u++)
                 if (n_samples[u])

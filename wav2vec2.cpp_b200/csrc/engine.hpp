@@ -142,6 +142,10 @@ private:
     bool fwd_begin(const BatchGeom& g, cudaStream_t st);
     void fwd_extract(const float* d_audio, const BatchGeom& g, int u0, int u1, cudaStream_t st);
     void fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, float* dbg_stages);
+    // fwd_extract over the whole batch + fwd_encode, from a captured graph when
+    // this (input, lengths) pair has been seen before (after fwd_begin).
+    void extract_encode(const float* d_audio, const BatchGeom& g, cudaStream_t st, float* dbg_feat,
+                        float* dbg_stages);
     // Launch bookkeeping: counts the launch and, when profiling, brackets it
     // with events attributed to category `cat` with `flops` algorithmic FLOPs.
     template <typename Fn> void launch(int cat, double flops, cudaStream_t st, const char* what, Fn fn);
