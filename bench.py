@@ -144,6 +144,8 @@ def workload_config(wl: Workload, world: int, lens_rot=None) -> dict:
     cfg["l2"] = ("L2 flushed (256 MB write) before every timed step; each step timed alone" if wl.flush_l2 else
                  f"inputs rotate over {wl.n_rot} distinct device batches (together > 126 MB L2); each step also "
                  f"streams >1 GB of activations")
+    cfg["launch"] = (f"each of the {wl.n_rot} input batches runs twice before the warm-up steps (the library captures "
+                     "the forward as a CUDA graph on its second sight of an input); timed steps replay the graphs")
     return cfg
 
 
@@ -400,6 +402,12 @@ def run_ours(args):
         m.forward_device(dev_batches[j % wl.n_rot].data_ptr(), lens_rot[j % wl.n_rot], stream.cuda_stream)
 
     with torch.cuda.stream(stream):
+        # The library captures the forward of a (device input, lengths) pair as
+        # a CUDA graph the second time it sees it and replays it after that:
+        # run every input batch twice before the warm-up steps, so that no
+        # capture falls inside the timed steps.
+        for j in range(2 * wl.n_rot):
+            step(j)
         for j in range(args.warmup):
             step(j)
     stream.synchronize()

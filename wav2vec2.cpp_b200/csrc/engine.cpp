@@ -480,9 +480,9 @@ void Engine::ensure_workspace(const BatchGeom& g) {
 }
 
 void Engine::drop_graphs() {
+    // the pairs already seen stay known: their next call captures afresh
     for (auto& e : graphs_) cudaGraphExecDestroy(e.exec);
     graphs_.clear();
-    graph_seen_.clear();
 }
 
 void Engine::upload_meta(const BatchGeom& g, cudaStream_t st) {
@@ -729,7 +729,10 @@ void Engine::extract_encode(const float* d_audio, const BatchGeom& g, cudaStream
         bool seen = false;
         for (auto& k : graph_seen_)
             if (k.first == d_audio && k.second == g.n_samples) seen = true;
-        if (seen) {
+        // A full cache captures nothing more (the calls run kernel by kernel):
+        // evicting would let a rotation over more inputs than it holds capture
+        // on every call.
+        if (seen && graphs_.size() < kMaxGraphs) {
             cudaGraph_t graph = nullptr;
             cuda_check(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
             try {
@@ -745,16 +748,14 @@ void Engine::extract_encode(const float* d_audio, const BatchGeom& g, cudaStream
             const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
             cudaGraphDestroy(graph);
             cuda_check(ie, "cudaGraphInstantiate");
-            if (graphs_.size() >= 8) {
-                cudaGraphExecDestroy(graphs_.front().exec);
-                graphs_.erase(graphs_.begin());
-            }
             graphs_.push_back({d_audio, g.n_samples, ws_gen_, exec, launches_last_});
             cuda_check(cudaGraphLaunch(exec, st), "cudaGraphLaunch");
             return;
         }
-        if (graph_seen_.size() >= 16) graph_seen_.erase(graph_seen_.begin());
-        graph_seen_.push_back({d_audio, g.n_samples});
+        if (!seen) {
+            if (graph_seen_.size() >= 4 * kMaxGraphs) graph_seen_.erase(graph_seen_.begin());
+            graph_seen_.push_back({d_audio, g.n_samples});
+        }
     }
     fwd_extract(d_audio, g, 0, g.n_utt, st);
     fwd_encode(g, st, dbg_feat, dbg_stages);

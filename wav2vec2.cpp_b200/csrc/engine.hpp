@@ -181,7 +181,8 @@ private:
     // Captured forwards (CUDA graphs) of Engine::forward, keyed by the input
     // pointer and the utterance lengths; valid while no workspace buffer is
     // reallocated (ws_gen_).  A geometry is captured the second time it is
-    // seen, so one-off batches and the first call's lazy set-up run eagerly.
+    // seen, so one-off batches and the first call's lazy set-up run eagerly;
+    // at most kMaxGraphs are kept (further pairs run kernel by kernel).
     struct GraphEntry {
         const float* audio;
         std::vector<int> n_samples;
@@ -189,6 +190,7 @@ private:
         cudaGraphExec_t exec;
         long long launches;
     };
+    static constexpr size_t kMaxGraphs = 16;
     std::vector<GraphEntry> graphs_;
     std::vector<std::pair<const float*, std::vector<int>>> graph_seen_;
     uint64_t ws_gen_ = 0;
