@@ -685,14 +685,25 @@ void Engine::fwd_encode(const BatchGeom& g, cudaStream_t st, float* dbg_feat, fl
         }
     } else {
         // pre-LN ("stable layer norm") encoder (src/wav2vec2.cpp:374-392)
+        // LayerNorm of x into the next GEMM's fp16 rows (the statistics pass:
+        // its (mean, rstd) output is not needed here)
+        auto ln_half = [&](const DevBuf& w, const DevBuf& b) {
+            if (H % 128) {   // the statistics pass takes rows of whole 128-column groups
+                ln_rows(x, nullptr, xh_.p, w, b);
+                return;
+            }
+            launch(P_LN, 0.0, st, "layer_norm", [&] {
+                return w2v_layer_norm_stats(x, M, H, w.as<float>(), b.as<float>(), xh_.p, lnstats_.as<float>(), st);
+            });
+        };
         dbg_copy(1, x);
         for (int l = 0; l < c.n_layers; l++) {
             const auto& L = layers_[l];
-            ln_rows(x, nullptr, xh_.p, L.ln1w, L.ln1b);
+            ln_half(L.ln1w, L.ln1b);
             plain_gemm(P_GEMM_ENC, xh_.p, L.qkv, qkv_.p, L.bqkv, nullptr, W2V_EPI_F16);
             attention();
             plain_gemm(P_GEMM_ENC, attn_.p, L.o, x, L.bo, x, W2V_EPI_F32_RESID);
-            ln_rows(x, nullptr, xh_.p, L.ln2w, L.ln2b);
+            ln_half(L.ln2w, L.ln2b);
             plain_gemm(P_GEMM_ENC, xh_.p, L.fc1, hbuf_.p, L.b1, nullptr, W2V_EPI_F16_GELU);
             plain_gemm(P_GEMM_ENC, hbuf_.p, L.fc2, x, L.b2, x, W2V_EPI_F32_RESID);
             if (l == c.n_layers - 1) ln_rows(x, x, xh_.p, enc_lnw_, enc_lnb_);
