@@ -653,7 +653,7 @@ def run_kernel_case(args):
           shape, K=768 -> N=3072, fp16 out, GELU epilogue);
     attention: 64 utterances x 499 frames, 12 heads x 64;
     pos_conv: the same batch, hidden 768, kernel 128, 16 groups;
-    layer_norm: M rows of 768 (fp32 in, fp16 + row statistics out)."""
+    layer_norm: M rows of --ln-dim (fp32 in, fp16 + row statistics out)."""
     import torch
     pkg()
     import w2v_b200.binding as b
@@ -706,7 +706,7 @@ def run_kernel_case(args):
         flops = 4.0 * B * T * T * H
     elif args.kernel == "layer_norm":
         # post-LN encoder LayerNorm: fp32 rows in, fp16 normalised rows + (mean, rstd) out
-        H, M = 768, args.rows
+        H, M = args.ln_dim, args.rows
         x = torch.randn(M, H, device="cuda")
         xh = torch.empty(M, H, device="cuda", dtype=torch.float16)
         stats = torch.empty(M, 2, device="cuda")
@@ -768,6 +768,7 @@ def main():
                          "4 fp32+LayerNorm-normalised residual)")
     ap.add_argument("--weights", choices=["f16", "q8_0", "q4_0"], default="f16",
                     help="B operand of --kernel gemm: fp16 rows, or quantised through the dequant-fused GEMM")
+    ap.add_argument("--ln-dim", type=int, default=768, help="row width for --kernel layer_norm")
     ap.add_argument("--block-n", type=int, default=0,
                     help="GEMM tile for --kernel gemm: 0 automatic, 64/128/256 one CTA, -128/-256 CTA pair")
     args = ap.parse_args()
