@@ -125,11 +125,13 @@ def test_gemm_q_matches_fp16_gemm(K, synth, gtype, M, N, Kd, epi, bn):
         assert (d <= 2e-5 * (1 + out_f.double().abs())).all(), d.max().item()
 
 
-@pytest.mark.parametrize("gtype,bn", [(Q8_0, -192), (Q4_0, -128), (Q8_0, 128), (Q8_0, 64), (Q4_0, -224)])
-def test_gemm_q_ln_resid(K, synth, gtype, bn):
+@pytest.mark.parametrize("gtype,bn,Kd", [(Q8_0, -192, 3072), (Q4_0, -128, 3072), (Q8_0, 128, 3072), (Q8_0, 64, 3072),
+                                         (Q4_0, -224, 3072), (Q8_0, -224, 768), (Q4_0, 128, 768), (Q8_0, 64, 768)])
+def test_gemm_q_ln_resid(K, synth, gtype, bn, Kd):
     """Post-LN residual epilogue (the residual normalised on the fly from
-    per-row statistics), in place over C."""
-    M, N, Kd = 3000, 768, 3072
+    per-row statistics), in place over C.  K <= 1024 runs two epilogue warps
+    per lane quarter (alternate chunks), K = 3072 one."""
+    M, N = 3000, 768
     q = QLinear(K, synth, N, Kd, gtype, 77)
     g = torch.Generator(device="cuda").manual_seed(9)
     A = torch.randn(M, Kd, device="cuda", generator=g).half()

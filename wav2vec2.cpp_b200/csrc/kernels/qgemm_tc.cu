@@ -41,8 +41,7 @@ namespace qg {
 
 constexpr int kBK = 64;             // K per k-block (128 bytes of fp16)
 constexpr int kRows = 128;          // weight rows per CTA (TMEM lanes)
-constexpr int kNE = 4, kNC = 4;     // epilogue / converter warps
-constexpr int kThreads = 64 + 32 * (kNE + kNC);
+constexpr int kNC = 4;              // converter warps (epilogue warps: QCfg::kNE)
 constexpr int kSmemCap = 232448;
 enum : int { kQ8 = 1, kQ4 = 2 };
 __host__ __device__ constexpr int code_row_bytes(int wq) { return wq == kQ8 ? 64 : 32; }
@@ -64,8 +63,11 @@ struct QParams {
     int* err;
 };
 
-template <int BN, int WQ, bool PAIR, int EPI>
+template <int BN, int WQ, bool PAIR, int EPI, int EH = 1>
 struct QCfg {
+    // EH epilogue warps per TMEM lane quarter (they take alternate 32-row chunks)
+    static constexpr int kNE = 4 * EH;
+    static constexpr int kThreads = 64 + 32 * (kNE + kNC);
     static constexpr int kXRows = PAIR ? BN / 2 : BN;          // activation rows one CTA stages
     static constexpr int kXBytes = kXRows * kBK * 2;
     static constexpr int kCodeBytes = kRows * code_row_bytes(WQ);
@@ -78,7 +80,7 @@ struct QCfg {
     // then per warp the current chunk's row statistics (256 B).
     static constexpr bool kRes = EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN;
     static constexpr int kOutBox = (EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU) ? 2048 : 4096;
-    static constexpr int kResBoxes = kRes ? 4 : 0;
+    static constexpr int kResBoxes = kRes ? (EH == 2 ? 2 : 4) : 0;
     static constexpr int kEpiWarp = 2 * kOutBox + kResBoxes * 4096;
     static constexpr int kEpiBytes = kNE * (kEpiWarp + 256);
     static constexpr int kStages = cmin(8, (kSmemCap - 1024 - 512 - kEpiBytes) / kPer);
@@ -91,7 +93,7 @@ struct QCfg {
     static constexpr int kACol = 2 * BN;                        // first weight-tile column
     static_assert(kStages >= 2 && kSB >= 2, "plan");
     static_assert(kXBytes % 1024 == 0 && kCodeBytes % 1024 == 0, "alignment");
-    static_assert((3 * kStages + 2 * kSB + 5 + kNE * (kResBoxes > 2 ? kResBoxes : 2)) * 8 + 4 <= 512, "barriers");
+    static_assert((3 * kStages + 2 * kSB + 5 + kNE * (kResBoxes > 1 ? kResBoxes : 1)) * 8 + 4 <= 512, "barriers");
 };
 
 // ── tcgen05 forms used only here ────────────────────────────────────────────
@@ -145,13 +147,13 @@ W2V_DEV void q4_word(uint32_t w, uint32_t dd, uint32_t* o) {
         o[j] = hmul2_u32(hsub2_u32(((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u, 0x64086408u), dd);
 }
 
-template <int BN, int EPI, int WQ, bool PAIR>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int EPI, int WQ, bool PAIR, int EH>
+__global__ void __launch_bounds__(QCfg<BN, WQ, PAIR, EPI, EH>::kThreads, 1)
 qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmQ,
              const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmC,
              const __grid_constant__ CUtensorMap tmR, QParams p) {
-    using Cfg = QCfg<BN, WQ, PAIR, EPI>;
-    constexpr int S = Cfg::kStages, SB = Cfg::kSB, CT = PAIR ? 2 : 1;
+    using Cfg = QCfg<BN, WQ, PAIR, EPI, EH>;
+    constexpr int S = Cfg::kStages, SB = Cfg::kSB, CT = PAIR ? 2 : 1, kNE = Cfg::kNE;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -353,8 +355,10 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
             }
         }
     } else {
-        // epilogue: lane = output feature, the 32 registers of a chunk = 32 activation rows
+        // epilogue: lane = output feature, the 32 registers of a chunk = 32 activation rows;
+        // with EH = 2 two warps share a lane quarter and take alternate chunks (eh, eh + 2, ...)
         const int q = warp & 3;
+        const int eh = (warp - 2) / 4;
         if (p.tma) {
             // Staged: per 32 x 32 chunk, the residual box arrives by TMA R - 1 chunks
             // ahead (a ring of R boxes per warp, the first R - 1 requested before the
@@ -404,25 +408,30 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                     tma_load_2d(rbox + b * 1024, &tmR, &rb[b], fcol0, ri * BN + c * 32);
                 };
                 const uint32_t rfirst = nrl;
-                int nreq = 0;                        // chunks of this tile whose residual is requested
+                // this warp's chunks: eh, eh + EH, ...; the residual of its k-th chunk goes
+                // to ring slot (rfirst + k) % R
+                int nreq = 0;                        // of this warp's chunks in this tile, residuals requested
+                auto chunk_ok = [&](int k) { return eh + k * EH < kNch && ri * BN + (eh + k * EH) * 32 < p.m_valid; };
                 if constexpr (kRes) {
-                    // chunks 0 .. R-2 before the accumulator is ready; chunk c + R - 1 at chunk c
-                    for (; nreq < (int)R - 1 && nreq < kNch && ri * BN + nreq * 32 < p.m_valid; nreq++) {
-                        if (lane == 0) request(nreq);
+                    // the first R-1 before the accumulator is ready; chunk k + R - 1 at chunk k
+                    for (; nreq < (int)R - 1 && chunk_ok(nreq); nreq++) {
+                        if (lane == 0) request(eh + nreq * EH);
                         nrl++;
                     }
                 }
                 float2 stn = make_float2(0.f, 0.f);
-                if (EPI == W2V_EPI_F32_RESID_LN && ri * BN + lane < p.m_valid) stn = p.ln_stats[ri * BN + lane];
+                if (EPI == W2V_EPI_F32_RESID_LN && ri * BN + eh * 32 + lane < p.m_valid)
+                    stn = p.ln_stats[ri * BN + eh * 32 + lane];
                 if (!mbar_wait(&tfull[ab], aph, p.err)) break;
                 tc_fence_after();
                 const uint32_t tacc = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * BN);
                 bool ok = true;
 #pragma unroll 1
-                for (int c = 0; c < kNch; c++) {
+                for (int c = eh, k = 0; c < kNch; c += EH, k++) {
                     float v[32];
                     tmem_ld32(tacc + (uint32_t)(c * 32), v);
-                    if (c == kNch - 1) {
+                    if (c + EH >= kNch) {
+                        // this warp's last chunk is in registers: its share of the accumulator is free
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) {
@@ -433,14 +442,14 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                     const int r0 = ri * BN + c * 32;
                     if (r0 >= p.m_valid) continue;
                     const float2 st = stn;
-                    if (EPI == W2V_EPI_F32_RESID_LN && c + 1 < kNch)
-                        stn = r0 + 32 + lane < p.m_valid ? p.ln_stats[r0 + 32 + lane] : make_float2(0.f, 0.f);
+                    if (EPI == W2V_EPI_F32_RESID_LN && c + EH < kNch)
+                        stn = r0 + 32 * EH + lane < p.m_valid ? p.ln_stats[r0 + 32 * EH + lane] : make_float2(0.f, 0.f);
                     const float* rcur = rbox;
                     if constexpr (kRes) {
-                        const uint32_t idx = rfirst + (uint32_t)c;
-                        if (nreq < kNch && ri * BN + nreq * 32 < p.m_valid) {
-                            __syncwarp();            // every lane is done with the box chunk nreq reuses (chunk c - 1's)
-                            if (lane == 0) request(nreq);
+                        const uint32_t idx = rfirst + (uint32_t)k;
+                        if (chunk_ok(nreq)) {
+                            __syncwarp();            // every lane is done with the box chunk nreq reuses (chunk k - 1's)
+                            if (lane == 0) request(eh + nreq * EH);
                             nrl++;
                             nreq++;
                         }
@@ -528,15 +537,15 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                 }
                 if (EPI == W2V_EPI_F32_RESID_LN) stn = r0 + lane < p.m_valid ? p.ln_stats[r0 + lane] : make_float2(0.f, 0.f);
             };
-            if (kRes) fetch(0);
+            if (kRes) fetch(eh);
             if (!mbar_wait(&tfull[ab], aph, p.err)) break;
             tc_fence_after();
             const uint32_t tacc = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * BN);
 #pragma unroll 1
-            for (int c = 0; c < kNch; c++) {
+            for (int c = eh; c < kNch; c += EH) {
                 float v[32];
                 tmem_ld32(tacc + (uint32_t)(c * 32), v);
-                if (c == kNch - 1) {
+                if (c + EH >= kNch) {
                     // the accumulator is in registers: hand it back to the MMA
                     tc_fence_before();
                     __syncwarp();
@@ -551,7 +560,7 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                 if constexpr (kRes) {
 #pragma unroll
                     for (int j = 0; j < 32; j++) rv[j] = rn[j];
-                    if (c + 1 < kNch && r0 + 32 < p.m_valid) fetch(c + 1);
+                    if (c + EH < kNch && r0 + 32 * EH < p.m_valid) fetch(c + EH);
                 }
                 if (r0 >= p.m_valid) continue;
                 if (EPI == W2V_EPI_F16 || EPI == W2V_EPI_F16_GELU) {
@@ -615,11 +624,11 @@ static int sm_count() {
     return n > 0 ? n : 148;
 }
 
-template <int BN, int EPI, int WQ, bool PAIR>
+template <int BN, int EPI, int WQ, bool PAIR, int EH = 1>
 static int launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts, const CUtensorMap& tc,
                   const CUtensorMap& tr, const QParams& p, cudaStream_t st) {
-    using Cfg = QCfg<BN, WQ, PAIR, EPI>;
-    auto kern = qgemm_kernel<BN, EPI, WQ, PAIR>;
+    using Cfg = QCfg<BN, WQ, PAIR, EPI, EH>;
+    auto kern = qgemm_kernel<BN, EPI, WQ, PAIR, EH>;
     static int max_units[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -629,7 +638,7 @@ static int launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMa
     attr[0].val.clusterDim.x = PAIR ? 2 : 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
     cfg.dynamicSmemBytes = Cfg::kSmem;
     cfg.stream = st;
     cfg.attrs = attr;
@@ -654,26 +663,34 @@ static int launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMa
     return cudaPeekAtLastError() == cudaSuccess ? W2V_OK : W2V_ERR_LAUNCH;
 }
 
-template <int EPI, int WQ>
+template <int EPI, int WQ, int EH>
 static int launch_tile(int bn, const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts,
                        const CUtensorMap& tc, const CUtensorMap& tr, const QParams& p, cudaStream_t st) {
     switch (bn) {
-        case -224: return launch<224, EPI, WQ, true>(tx, tq, ts, tc, tr, p, st);
-        case 224: return launch<224, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
-        case -192: return launch<192, EPI, WQ, true>(tx, tq, ts, tc, tr, p, st);
-        case -128: return launch<128, EPI, WQ, true>(tx, tq, ts, tc, tr, p, st);
-        case 192: return launch<192, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
-        case 128: return launch<128, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
-        case 64: return launch<64, EPI, WQ, false>(tx, tq, ts, tc, tr, p, st);
+        case -224: return launch<224, EPI, WQ, true, EH>(tx, tq, ts, tc, tr, p, st);
+        case 224: return launch<224, EPI, WQ, false, EH>(tx, tq, ts, tc, tr, p, st);
+        case -192: return launch<192, EPI, WQ, true, EH>(tx, tq, ts, tc, tr, p, st);
+        case -128: return launch<128, EPI, WQ, true, EH>(tx, tq, ts, tc, tr, p, st);
+        case 192: return launch<192, EPI, WQ, false, EH>(tx, tq, ts, tc, tr, p, st);
+        case 128: return launch<128, EPI, WQ, false, EH>(tx, tq, ts, tc, tr, p, st);
+        case 64: return launch<64, EPI, WQ, false, EH>(tx, tq, ts, tc, tr, p, st);
         default: return W2V_ERR_ARGS;
     }
 }
 
+// eh = 2: two epilogue warps per lane quarter, for the residual epilogues of
+// short-K linears (the out-projection), whose tiles finish their MMAs before
+// one warp per quarter can drain the fp32 output and residual
 template <int EPI>
-static int launch_w(int wq, int bn, const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts,
+static int launch_w(int wq, int bn, int eh, const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts,
                     const CUtensorMap& tc, const CUtensorMap& tr, const QParams& p, cudaStream_t st) {
-    return wq == kQ8 ? launch_tile<EPI, kQ8>(bn, tx, tq, ts, tc, tr, p, st)
-                     : launch_tile<EPI, kQ4>(bn, tx, tq, ts, tc, tr, p, st);
+    if constexpr (EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) {
+        if (eh == 2)
+            return wq == kQ8 ? launch_tile<EPI, kQ8, 2>(bn, tx, tq, ts, tc, tr, p, st)
+                             : launch_tile<EPI, kQ4, 2>(bn, tx, tq, ts, tc, tr, p, st);
+    }
+    return wq == kQ8 ? launch_tile<EPI, kQ8, 1>(bn, tx, tq, ts, tc, tr, p, st)
+                     : launch_tile<EPI, kQ4, 1>(bn, tx, tq, ts, tc, tr, p, st);
 }
 
 // Tile: CTA pairs (256 weight rows per tile) or single CTAs (128), each over
@@ -806,12 +823,13 @@ static int qgemm_impl(const void* A, long long K, long long M, const void* Bq, c
     p.ln_b = ln_b;
     p.err = err;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int eh = res && tma && K <= 1024 ? 2 : 1;
     switch (epilogue) {
-        case W2V_EPI_F16: return launch_w<W2V_EPI_F16>(wq, bn, tx, tq, ts, tc, tr, p, st);
-        case W2V_EPI_F16_GELU: return launch_w<W2V_EPI_F16_GELU>(wq, bn, tx, tq, ts, tc, tr, p, st);
-        case W2V_EPI_F32: return launch_w<W2V_EPI_F32>(wq, bn, tx, tq, ts, tc, tr, p, st);
-        case W2V_EPI_F32_RESID: return launch_w<W2V_EPI_F32_RESID>(wq, bn, tx, tq, ts, tc, tr, p, st);
-        default: return launch_w<W2V_EPI_F32_RESID_LN>(wq, bn, tx, tq, ts, tc, tr, p, st);
+        case W2V_EPI_F16: return launch_w<W2V_EPI_F16>(wq, bn, 1, tx, tq, ts, tc, tr, p, st);
+        case W2V_EPI_F16_GELU: return launch_w<W2V_EPI_F16_GELU>(wq, bn, 1, tx, tq, ts, tc, tr, p, st);
+        case W2V_EPI_F32: return launch_w<W2V_EPI_F32>(wq, bn, 1, tx, tq, ts, tc, tr, p, st);
+        case W2V_EPI_F32_RESID: return launch_w<W2V_EPI_F32_RESID>(wq, bn, eh, tx, tq, ts, tc, tr, p, st);
+        default: return launch_w<W2V_EPI_F32_RESID_LN>(wq, bn, eh, tx, tq, ts, tc, tr, p, st);
     }
 }
 
