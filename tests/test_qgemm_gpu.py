@@ -129,8 +129,9 @@ def test_gemm_q_matches_fp16_gemm(K, synth, gtype, M, N, Kd, epi, bn):
                                          (Q4_0, -224, 3072), (Q8_0, -224, 768), (Q4_0, 128, 768), (Q8_0, 64, 768)])
 def test_gemm_q_ln_resid(K, synth, gtype, bn, Kd):
     """Post-LN residual epilogue (the residual normalised on the fly from
-    per-row statistics), in place over C.  K <= 1024 runs two epilogue warps
-    per lane quarter (alternate chunks), K = 3072 one."""
+    per-row statistics), in place over C, with two epilogue warps per lane
+    quarter on alternate chunks (and one where the output cannot take TMA
+    stores)."""
     M, N = 3000, 768
     q = QLinear(K, synth, N, Kd, gtype, 77)
     g = torch.Generator(device="cuda").manual_seed(9)

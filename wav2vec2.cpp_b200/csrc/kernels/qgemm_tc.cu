@@ -678,13 +678,16 @@ static int launch_tile(int bn, const CUtensorMap& tx, const CUtensorMap& tq, con
     }
 }
 
-// eh = 2: two epilogue warps per lane quarter, for the residual epilogues of
-// short-K linears (the out-projection), whose tiles finish their MMAs before
-// one warp per quarter can drain the fp32 output and residual
+// eh = 2: two epilogue warps per lane quarter for the heavier epilogues (the
+// fp32 residual ones and fp16 + GELU).  Measured at 31936 rows: the
+// out-projection's LayerNorm residual 580 -> 688 TFLOP/s (its tiles finish
+// their MMAs, K = 768, before one warp per quarter drains them), FFN-up + GELU
+// 1013 -> 1040, FFN-down 1022 -> 1030; plain fp16 (QKV) unchanged, so it
+// keeps one.
 template <int EPI>
 static int launch_w(int wq, int bn, int eh, const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts,
                     const CUtensorMap& tc, const CUtensorMap& tr, const QParams& p, cudaStream_t st) {
-    if constexpr (EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN) {
+    if constexpr (EPI == W2V_EPI_F32_RESID || EPI == W2V_EPI_F32_RESID_LN || EPI == W2V_EPI_F16_GELU) {
         if (eh == 2)
             return wq == kQ8 ? launch_tile<EPI, kQ8, 2>(bn, tx, tq, ts, tc, tr, p, st)
                              : launch_tile<EPI, kQ4, 2>(bn, tx, tq, ts, tc, tr, p, st);
@@ -823,10 +826,10 @@ static int qgemm_impl(const void* A, long long K, long long M, const void* Bq, c
     p.ln_b = ln_b;
     p.err = err;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int eh = res && tma && K <= 1024 ? 2 : 1;
+    const int eh = tma ? 2 : 1;   // used by the residual and GELU epilogues (launch_w)
     switch (epilogue) {
         case W2V_EPI_F16: return launch_w<W2V_EPI_F16>(wq, bn, 1, tx, tq, ts, tc, tr, p, st);
-        case W2V_EPI_F16_GELU: return launch_w<W2V_EPI_F16_GELU>(wq, bn, 1, tx, tq, ts, tc, tr, p, st);
+        case W2V_EPI_F16_GELU: return launch_w<W2V_EPI_F16_GELU>(wq, bn, eh, tx, tq, ts, tc, tr, p, st);
         case W2V_EPI_F32: return launch_w<W2V_EPI_F32>(wq, bn, 1, tx, tq, ts, tc, tr, p, st);
         case W2V_EPI_F32_RESID: return launch_w<W2V_EPI_F32_RESID>(wq, bn, eh, tx, tq, ts, tc, tr, p, st);
         default: return launch_w<W2V_EPI_F32_RESID_LN>(wq, bn, eh, tx, tq, ts, tc, tr, p, st);
