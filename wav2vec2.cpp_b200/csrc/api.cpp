@@ -196,6 +196,10 @@ void run_sharded(wav2vec2_context* ctx, const float* const* samples, const int* 
                  bool want_logits, bool want_spans, Fn fn) {
     const auto batches = make_batches(n_samples, n_utt, ctx->max_batch, (long long)ctx->max_batch * 16000LL * 32);
     const int nw = (int)std::min(ctx->engines.size(), std::max<size_t>(batches.size(), 1));
+    // the devices' packing threads share the host: half its hardware threads
+    // in all, at most 8 per device
+    const int hw = (int)std::max(1u, std::thread::hardware_concurrency());
+    for (int w = 0; w < nw; w++) ctx->engines[w]->set_pack_threads(std::max(1, std::min(8, hw / (2 * nw))));
     run_batches(batches.size(), nw, [&](int w, size_t bi, std::string& err) {
         Engine* e = ctx->engines[w].get();
         std::vector<float> logits;

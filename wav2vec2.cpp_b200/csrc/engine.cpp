@@ -806,7 +806,7 @@ void Engine::run_host(const std::vector<const float*>& audio, const std::vector<
         for (int k = 2; k <= nch; k++) cu[k] = cu[1] + (int)((long long)(B - cu[1]) * (k - 1) / (nch - 1));
     }
     const int hw = (int)std::max(1u, std::thread::hardware_concurrency());
-    const int nt = std::max(1, std::min({8, hw / 2, std::max(1, B / nch)}));
+    const int nt = std::max(1, std::min({pack_threads_ > 0 ? pack_threads_ : 8, hw / 2, std::max(1, B / nch)}));
     std::unique_ptr<std::atomic<int>[]> packed(new std::atomic<int>[nch]);
     for (int k = 0; k < nch; k++) packed[k].store(0);
     auto pack = [&](int t) {

@@ -95,6 +95,9 @@ public:
 
     // Host-memory convenience used by the C API: packs the utterances into
     // pinned memory, uploads, runs forward, downloads logits and/or spans.
+    // Host threads that pack one batch's pageable audio (0: up to 8, half the
+    // host's hardware threads); a context over several devices divides them.
+    void set_pack_threads(int n) { pack_threads_ = n; }
     void run_host(const std::vector<const float*>& audio, const std::vector<int>& n_samples,
                   std::vector<float>* logits, std::vector<int>* spans, std::vector<int>* n_spans,
                   BatchGeom* geom_out);
@@ -195,6 +198,7 @@ private:
     std::vector<std::pair<const float*, std::vector<int>>> graph_seen_;
     uint64_t ws_gen_ = 0;
     bool graphs_enabled_ = true;   // W2V_B200_GRAPHS=0: always launch kernel by kernel
+    int pack_threads_ = 0;
     void drop_graphs();
 
     struct ProfRec { int cat; cudaEvent_t a, b; double flops; };
