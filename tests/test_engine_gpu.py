@@ -274,6 +274,35 @@ def test_forward_device_graph_replays_equal_eager(W, model_path, synth, monkeypa
     me.close()
 
 
+def test_graph_cache_beyond_capacity_runs_eagerly(W, model_path, synth, monkeypatch):
+    """More (input, lengths) pairs than the capture cache holds (16): the
+    pairs past capacity run kernel by kernel, and every call, replayed or
+    not, equals a model that never captures."""
+    p = model_path("tiny", "q8_0", bias_std=0.02, gain_jitter=0.1)
+    m = W.Model(p)
+    monkeypatch.setenv("W2V_B200_GRAPHS", "0")
+    me = W.Model(p)
+    monkeypatch.delenv("W2V_B200_GRAPHS")
+    V = m.cfg["vocab"]
+    s = torch.cuda.Stream()
+
+    def run(model, d, lens):
+        with torch.cuda.stream(s):
+            model.forward_device(d.data_ptr(), lens, s.cuda_stream)
+        s.synchronize()
+        lg_ptr, _, _, M = model.device_outputs()
+        return torch.as_tensor(_DevArray(lg_ptr, M * V, "<f4"), device="cuda").cpu().numpy().copy()
+
+    big = torch.from_numpy(synth.make_audio(16000 * 4, 77)).cuda()   # one input address
+    keys = [[16000 + 400 * i] for i in range(20)]   # 20 lengths; the workspace stops growing after the first pass
+    refs = [run(me, big, k) for k in keys]
+    for _ in range(3):
+        for k, ref in zip(keys, refs):
+            assert np.array_equal(run(m, big, k), ref)
+    m.close()
+    me.close()
+
+
 def test_host_path_graph_replays_equal_eager(W, model_path, synth, monkeypatch):
     """Host batches of fewer than 8 utterances upload in one piece and then
     run the forward through the same capture/replay cache: repeated calls
