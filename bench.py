@@ -625,7 +625,9 @@ def run_sweep(args):
            "config": {"workload": f"wav2vec2-base Q8_0 (seeded random init), {len(lens)} utterances, lengths "
                                   f"seeded uniform {wl.ragged[0]:g}-{wl.ragged[1]:g} s, length-bucketed into "
                                   f"batches of <= {wl.batch} by the library, one context over {n_dev} device(s)",
-                      "api": "wav2vec2_transcribe_batch (pageable host float32 in, text out)"}}
+                      "api": "wav2vec2_transcribe_batch (pageable host float32 in, text out)",
+                      "busy": "per device, the device time of its batches summed over its engines (two per device "
+                              "on a context over several devices, whose batches overlap: the fraction may exceed 1)"}}
     sampler = ClockSampler("0")
     sampler.start()
     for beam in (1, 5):

@@ -326,6 +326,27 @@ def test_host_path_graph_replays_equal_eager(W, model_path, synth, monkeypatch):
     me.close()
 
 
+def test_multi_engine_context_matches_single(W, model_path, synth):
+    """A context over two devices (here both device 0) runs two engines per
+    device as batch workers -- four engines sharing one GPU, each with its own
+    stream and workspace -- and the length-bucketed, sharded batch call gives
+    the transcripts and logits of a one-device context."""
+    p = model_path("tiny", "q8_0", bias_std=0.02, gain_jitter=0.1)
+    one = W.Model(p, max_batch=4)
+    four = W.Model(p, devices=[0, 0], max_batch=4)
+    lens = [16000, 7000, 12000, 3000, 9000, 16000, 400, 5000, 8000, 11000, 2000, 14000, 6000, 10000, 4000, 15000]
+    xs = [synth.make_audio(n, 300 + i) for i, n in enumerate(lens)]
+    a = one.transcribe_batch(xs, word_timestamps=True)
+    b = four.transcribe_batch(xs, word_timestamps=True)
+    assert [(r["text"], r["words"]) for r in a] == [(r["text"], r["words"]) for r in b]
+    la, lb = one.logits(xs), four.logits(xs)
+    assert all(np.array_equal(u, v) for u, v in zip(la, lb))
+    st = four.device_stats()
+    assert len(st) == 2 and sum(d["batches"] for d in st) >= 4
+    one.close()
+    four.close()
+
+
 def test_init_rejects_bad_model(W, tmp_path):
     bad = tmp_path / "bad.gguf"
     bad.write_bytes(b"GGUF" + b"\0" * 10)

@@ -35,7 +35,13 @@ using namespace w2v;
 
 struct wav2vec2_context {
     ModelConfig cfg;
-    std::vector<std::unique_ptr<Engine>> engines;
+    std::vector<std::unique_ptr<Engine>> engines;   // one per device
+    // Batch workers for wav2vec2_transcribe_batch: the engines above, plus, on
+    // contexts over several devices, a second engine per device (its own
+    // stream and workspace), so that one engine packs and uploads its next
+    // batch while the other's kernels run.
+    std::vector<Engine*> workers;
+    std::vector<std::unique_ptr<Engine>> extra;
     int max_batch = 64;
 };
 
@@ -195,13 +201,13 @@ template <typename Fn>
 void run_sharded(wav2vec2_context* ctx, const float* const* samples, const int* n_samples, int n_utt,
                  bool want_logits, bool want_spans, Fn fn) {
     const auto batches = make_batches(n_samples, n_utt, ctx->max_batch, (long long)ctx->max_batch * 16000LL * 32);
-    const int nw = (int)std::min(ctx->engines.size(), std::max<size_t>(batches.size(), 1));
-    // the devices' packing threads share the host: half its hardware threads
-    // in all, at most 8 per device
+    const int nw = (int)std::min(ctx->workers.size(), std::max<size_t>(batches.size(), 1));
+    // the workers' packing threads share the host: half its hardware threads
+    // in all, at most 8 per worker
     const int hw = (int)std::max(1u, std::thread::hardware_concurrency());
-    for (int w = 0; w < nw; w++) ctx->engines[w]->set_pack_threads(std::max(1, std::min(8, hw / (2 * nw))));
+    for (int w = 0; w < nw; w++) ctx->workers[w]->set_pack_threads(std::max(1, std::min(8, hw / (2 * nw))));
     run_batches(batches.size(), nw, [&](int w, size_t bi, std::string& err) {
-        Engine* e = ctx->engines[w].get();
+        Engine* e = ctx->workers[w];
         std::vector<float> logits;
         std::vector<int> spans, nsp;
         const auto& b = batches[bi];
@@ -263,6 +269,14 @@ wav2vec2_context* wav2vec2_b200_init(const char* path, const int* devices, int n
             if (d < 0 || d >= avail) throw std::runtime_error("invalid device index " + std::to_string(d));
             ctx->engines.push_back(std::make_unique<Engine>(gf, ctx->cfg, d));
         }
+        int per_device = n_devices > 1 ? 2 : 1;
+        if (const char* s = getenv("W2V_B200_ENGINES_PER_DEVICE")) per_device = std::max(1, std::min(4, atoi(s)));
+        for (auto& e : ctx->engines) ctx->workers.push_back(e.get());
+        for (int k = 1; k < per_device; k++)
+            for (int i = 0; i < n_devices; i++) {
+                ctx->extra.push_back(std::make_unique<Engine>(gf, ctx->cfg, ctx->engines[i]->device()));
+                ctx->workers.push_back(ctx->extra.back().get());
+            }
         return ctx.release();
     } catch (const std::exception& e) {
         set_error(e.what());
@@ -517,15 +531,24 @@ int wav2vec2_b200_ctc_beam_search(const float* logits, int T, int V, int blank, 
 int wav2vec2_b200_device_stats(wav2vec2_context* ctx, int reset, double* busy_ms, long long* batches,
                                long long* samples, int cap) {
     if (!ctx || cap < 0) return -1;
-    const int n = std::min<int>(cap, (int)ctx->engines.size());
-    for (int i = 0; i < (int)ctx->engines.size(); i++) {
+    // per device: the sums over its engines (a second engine's batches overlap
+    // the first's, so busy_ms may exceed the wall time)
+    const int nd = (int)ctx->engines.size();
+    const int n = std::min<int>(cap, nd);
+    for (int i = 0; i < n; i++) {
+        if (busy_ms) busy_ms[i] = 0;
+        if (batches) batches[i] = 0;
+        if (samples) samples[i] = 0;
+    }
+    for (size_t k = 0; k < ctx->workers.size(); k++) {
         double ms = 0;
         long long nb = 0, ns = 0;
-        ctx->engines[i]->busy_stats(&ms, &nb, &ns, reset != 0);
+        ctx->workers[k]->busy_stats(&ms, &nb, &ns, reset != 0);
+        const int i = (int)(k % (size_t)nd);
         if (i < n) {
-            if (busy_ms) busy_ms[i] = ms;
-            if (batches) batches[i] = nb;
-            if (samples) samples[i] = ns;
+            if (busy_ms) busy_ms[i] += ms;
+            if (batches) batches[i] += nb;
+            if (samples) samples[i] += ns;
         }
     }
     return n;
