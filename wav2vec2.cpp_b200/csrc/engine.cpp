@@ -744,24 +744,32 @@ void Engine::extract_encode(const float* d_audio, const BatchGeom& g, cudaStream
         // evicting would let a rotation over more inputs than it holds capture
         // on every call.
         if (seen && graphs_.size() < kMaxGraphs) {
+            // Nothing captured is launched until the graph is instantiated: if the
+            // capture or the instantiation fails, this engine stops capturing and
+            // runs the forward kernel by kernel (a real error then surfaces there).
             cudaGraph_t graph = nullptr;
-            cuda_check(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
-            try {
-                fwd_extract(d_audio, g, 0, g.n_utt, st);
-                fwd_encode(g, st, nullptr, nullptr);
-            } catch (...) {
-                cudaStreamEndCapture(st, &graph);
-                if (graph) cudaGraphDestroy(graph);
-                throw;
-            }
-            cuda_check(cudaStreamEndCapture(st, &graph), "cudaStreamEndCapture");
             cudaGraphExec_t exec = nullptr;
-            const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
-            cudaGraphDestroy(graph);
-            cuda_check(ie, "cudaGraphInstantiate");
-            graphs_.push_back({d_audio, g.n_samples, ws_gen_, exec, launches_last_});
-            cuda_check(cudaGraphLaunch(exec, st), "cudaGraphLaunch");
-            return;
+            bool captured = false;
+            if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+                try {
+                    fwd_extract(d_audio, g, 0, g.n_utt, st);
+                    fwd_encode(g, st, nullptr, nullptr);
+                    captured = true;
+                } catch (...) {
+                }
+                if (cudaStreamEndCapture(st, &graph) != cudaSuccess) captured = false;
+                if (captured && cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) captured = false;
+                if (graph) cudaGraphDestroy(graph);
+            }
+            if (captured) {
+                graphs_.push_back({d_audio, g.n_samples, ws_gen_, exec, launches_last_});
+                cuda_check(cudaGraphLaunch(exec, st), "cudaGraphLaunch");
+                return;
+            }
+            if (exec) cudaGraphExecDestroy(exec);
+            cudaGetLastError();
+            graphs_enabled_ = false;
+            launches_cur_ = 0;   // the abandoned capture counted its launches
         }
         if (!seen) {
             if (graph_seen_.size() >= 4 * kMaxGraphs) graph_seen_.erase(graph_seen_.begin());
