@@ -304,12 +304,12 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
         for (int tile = unit; tile < total && ok; tile += n_units) {
             for (int kb = 0; kb < p.k_blocks; kb++, kq++) {
                 const int s = kq % S, f = kq % SB;
-                if (!mbar_wait(&cfull[s], (uint32_t)(kq / S) & 1u, p.err) ||
-                    !mbar_wait(&aempty[f], ((uint32_t)(kq / SB) & 1u) ^ 1u, p.err)) {
+                if (!mbar_wait(&cfull[s], (uint32_t)(kq / S) & 1u, p.err)) {
                     ok = false;
                     break;
                 }
-                tc_fence_after();   // the MMA that read weight tile f has completed
+                // expand first, then wait for the MMA to release weight tile f: only the
+                // TMEM store stays between that release and the next k-block's MMA
                 const uint16_t* sc = reinterpret_cast<const uint16_t*>(sS + s * Cfg::kScaleBytes);
                 const uint32_t d0 = sc[fl], d1 = sc[kRows + fl];
                 const uint32_t dd0 = d0 | (d0 << 16), dd1 = d1 | (d1 << 16);
@@ -344,6 +344,11 @@ qgemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CU
                     q4_word(c[1].z, dd1, v + 24);
                     q4_word(c[1].w, dd1, v + 28);
                 }
+                if (!mbar_wait(&aempty[f], ((uint32_t)(kq / SB) & 1u) ^ 1u, p.err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();   // the MMA that read weight tile f has completed
                 tmem_st32u(trow + (uint32_t)(f * 32), v);
                 tmem_wait_st();
                 tc_fence_before();
