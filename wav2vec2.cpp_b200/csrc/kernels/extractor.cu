@@ -667,6 +667,136 @@ __global__ void __launch_bounds__(128) conv0x4_apply_kernel(Conv0Args a) {
     }
 }
 
+// Conv layer 0 + LayerNorm over its 512 channels + GELU, for the LayerNorm
+// feature extractor (wav2vec2-large / XLS-R: src/wav2vec2.cpp:273-287 with
+// src/ops.h:24-36) at the published shape (10 taps, stride 5, 512 channels).
+// A warp owns whole frames, so the per-frame LayerNorm needs only warp
+// shuffles: lane l holds channel pairs p = l + 32 j (channels 2p, 2p+1,
+// j = 0..7) of kLnF = 4 frames at a time.  The 10 x 512 weights and the bias
+// sit in shared memory as pairs (one conflict-free 8-byte read serves 4
+// frames x 2 channels), the samples of the block's frames are staged once
+// normalised, and the convolution runs as packed fp32-pair FMAs.  Two-pass
+// statistics in fp32 as the reference; GELU on fp16 pairs (gelu_f16x2) as the
+// tensor-core conv 0 does, since the output is fp16.
+constexpr int kLnF = 4;                   // frames per register group
+constexpr int kLnThreads = 128;           // 4 warps
+constexpr int kLnBlockFrames = 512;       // frames per block: 128 per warp
+constexpr int kLnC = 512;
+constexpr int kLnSamples = (kLnBlockFrames - 1) * kC0S + kC0K;   // 2565
+
+__global__ void __launch_bounds__(kLnThreads, 3) conv0_ln_kernel(Conv0Args a) {
+    __shared__ uint64_t ws[kC0K][kLnC / 2];   // (w[2p][k], w[2p+1][k])
+    __shared__ uint64_t wb[kLnC / 2];         // (b[2p], b[2p+1])
+    __shared__ float xs[kLnSamples + kLnF * kC0S];
+    const int u = blockIdx.y;
+    const int F = a.frames[u];
+    const int f0 = blockIdx.x * kLnBlockFrames;
+    if (f0 >= F) return;
+    const int nf = min(kLnBlockFrames, F - f0);
+    {
+        const float mean = a.stats[2 * u], inv = a.stats[2 * u + 1];
+        const float* x = a.audio + a.off[u] + (long long)f0 * kC0S;
+        const int ns = (nf - 1) * kC0S + kC0K;
+        for (int i = threadIdx.x; i < kLnSamples + kLnF * kC0S; i += kLnThreads)
+            xs[i] = i < ns ? (x[i] - mean) * inv : 0.f;
+        for (int i = threadIdx.x; i < kC0K * kLnC / 2; i += kLnThreads) {
+            const int k = i / (kLnC / 2), p = i % (kLnC / 2);
+            ws[k][p] = f32x2(__ldg(a.w0 + (2 * p) * kC0K + k), __ldg(a.w0 + (2 * p + 1) * kC0K + k));
+        }
+        for (int p = threadIdx.x; p < kLnC / 2; p += kLnThreads)
+            wb[p] = a.b0 ? f32x2(__ldg(a.b0 + 2 * p), __ldg(a.b0 + 2 * p + 1)) : 0ull;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t g2[8], b2[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int c = 2 * (lane + 32 * j);
+        g2[j] = f32x2(__ldg(a.gw + c), __ldg(a.gw + c + 1));
+        b2[j] = f32x2(__ldg(a.gb + c), __ldg(a.gb + c + 1));
+    }
+    constexpr float kInvC = 1.f / kLnC;
+    const int wf0 = warp * (kLnBlockFrames / 4);
+    __half* orow = a.out + ((long long)u * a.rows_max + f0) * kLnC;
+#pragma unroll 1
+    for (int g = wf0; g < wf0 + kLnBlockFrames / 4 && g < nf; g += kLnF) {
+        uint64_t acc[kLnF][8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint64_t b = wb[lane + 32 * j];
+#pragma unroll
+            for (int f = 0; f < kLnF; f++) acc[f][j] = b;
+        }
+#pragma unroll 1
+        for (int k = 0; k < kC0K; k++) {
+            uint64_t xk[kLnF];
+#pragma unroll
+            for (int f = 0; f < kLnF; f++) {
+                const float v = xs[(g + f) * kC0S + k];
+                xk[f] = f32x2(v, v);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint64_t w = ws[k][lane + 32 * j];
+#pragma unroll
+                for (int f = 0; f < kLnF; f++) acc[f][j] = fma_f32x2(xk[f], w, acc[f][j]);
+            }
+        }
+        // the four frames' reductions interleaved (independent shuffle chains);
+        // frames past the block's last are computed on zeros and not stored
+        float mean[kLnF], r[kLnF];
+#pragma unroll
+        for (int f = 0; f < kLnF; f++) {
+            uint64_t s2 = acc[f][0];
+#pragma unroll
+            for (int j = 1; j < 8; j++) s2 = add_f32x2(s2, acc[f][j]);
+            float lo, hi;
+            f32x2_split(s2, lo, hi);
+            mean[f] = lo + hi;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int f = 0; f < kLnF; f++) mean[f] += __shfl_xor_sync(0xffffffffu, mean[f], o);
+#pragma unroll
+        for (int f = 0; f < kLnF; f++) {
+            mean[f] *= kInvC;
+            const uint64_t nm2 = f32x2(-mean[f], -mean[f]);
+            uint64_t q2 = 0ull;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                acc[f][j] = add_f32x2(acc[f][j], nm2);   // centred in place
+                q2 = fma_f32x2(acc[f][j], acc[f][j], q2);
+            }
+            float lo, hi;
+            f32x2_split(q2, lo, hi);
+            r[f] = lo + hi;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int f = 0; f < kLnF; f++) r[f] += __shfl_xor_sync(0xffffffffu, r[f], o);
+#pragma unroll
+        for (int f = 0; f < kLnF; f++) {
+            if (g + f >= nf) break;
+            const float rf = 1.f / sqrtf(r[f] * kInvC + 1e-5f);
+            const uint64_t r2 = f32x2(rf, rf);
+            uint32_t* dst = reinterpret_cast<uint32_t*>(orow + (long long)(g + f) * kLnC) + lane;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint64_t y2 = fma_f32x2(fma_f32x2(acc[f][j], r2, 0ull), g2[j], b2[j]);
+                float lo, hi;
+                f32x2_split(y2, lo, hi);
+                dst[32 * j] = gelu_half2(lo, hi);
+            }
+        }
+    }
+}
+
+static bool conv0_ln_supported(int C, int k0, int s0, int norm, const void* out) {
+    return norm == 2 && C == kLnC && k0 == kC0K && s0 == kC0S && (reinterpret_cast<uintptr_t>(out) & 3) == 0;
+}
+
 // Vectorised row LayerNorm: warp per row, each lane holds NV groups of 4
 // consecutive columns (D = 128 * NV); 16-byte fp32 / 8-byte fp16 accesses.
 template <int NV>
@@ -920,6 +1050,11 @@ extern "C" int w2v_conv0(const float* audio, const long long* off, const int* le
     Conv0Args a{audio, off, len, frames, stats, w0, b0, C, k0, s0, norm, gw, gb, gn_sums, (__half*)out, rows_max,
                 nullptr};
     const bool k10 = k0 == 10;
+    if (conv0_ln_supported(C, k0, s0, norm, out)) {
+        dim3 g((max_frames + kLnBlockFrames - 1) / kLnBlockFrames, n_utt);
+        conv0_ln_kernel<<<g, kLnThreads, 0, S(stream)>>>(a);
+        return launch_rc();
+    }
     if (k0 == kC0K && s0 == kC0S && C % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0) {
         // published shape: 4 channels per thread, 8-frame register windows
         if (norm == 1) {
